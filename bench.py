@@ -1,0 +1,458 @@
+"""Benchmark of the B200 Gated DeltaNet operator pair (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed = rank):
+  * headline step: one decode step at B=64 (state [64,8,128,128] fp32, updated in place).
+    value = whole-job state HBM GB/s = N * 67,108,864 B / (max over ranks of the device time per step).
+    Timed as CUDA-graph replays of K decode launches cycling over 8 state buffers
+    (8 x 32 MiB = 256 MiB > the 126 MB L2, so every launch streams its state from HBM).
+  * prefill_8k: one 8192-token sequence (cu_seqlens = [0, 8192], initial state N(0, 0.02)),
+    tokens/s; L2 flushed (256 MiB write) before every timed step, per-step CUDA events.
+  * e2e: the same two metrics through the public API (gdn.decode.kernel / gdn.prefill.kernel)
+    with pinned host buffers: every step copies its inputs host->device and its results back.
+  * cpu_baseline: the CPU oracle (a C restatement of the reference's sequential PyTorch
+    loops, all host threads) on a bounded sample of the same workload, rank 0 only.
+--impl reference times that same CPU oracle as the reference arm (the reference itself is
+Python-only and cannot be installed on the GPU box, so its algorithm runs as the C port).
+Multi-GPU: one process per GPU under torchrun; no collective on the data path, a barrier and
+a MAX all-reduce of the timings only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "gated-delta-network_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode µs/step + state HBM GB/s at B=64; prefill tokens/s at 8K tokens"
+H, HV, D = 4, 8, 128
+DECODE_B = 64
+PREFILL_T = 8192
+STATE_BYTES_PER_ELEM = HV * D * D * 4                     # 524,288 B of fp32 state per batch element
+DECODE_STATE_BYTES = DECODE_B * STATE_BYTES_PER_ELEM * 2  # read + write = 67,108,864 B
+# algorithmic bytes of one decode launch: state r+w, q,k (2x4x128 bf16), v,out (2x8x128 bf16), a,b, A_log, dt_bias
+DECODE_ALG_BYTES = DECODE_B * (2 * STATE_BYTES_PER_ELEM + 2 * H * D * 2 + 2 * HV * D * 2 + 2 * HV * 2) + 2 * HV * 4
+# prefill: per token q,k (2x4x128 bf16) + v (8x128 bf16) + a,b (2x8 bf16) + out (8x128 bf16); per sequence state in+out
+PREFILL_ALG_BYTES_PER_TOKEN = 2 * H * D * 2 + HV * D * 2 + 2 * HV * 2 + HV * D * 2   # 6,176 B
+PREFILL_FLOPS_PER_TOKEN = (10 * 64 * 128 + 6 * 128 * 128) * HV                      # chunked WY form, 1,441,792
+N_STATE_BUFS = 8
+# DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum), or None.
+# Source: the ncu summaries under profiles/ (decode B=64 launch; prefill kernels at T=8192).
+NCU_TRAFFIC = {"decode": None, "prefill_scan": None}
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxs.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def cpu_decode_baseline(budget_s=10.0, threads=0):
+    """CPU oracle on decode B=64 (same inputs as the headline), repeated for ~budget_s."""
+    from oracle import oracle
+    from tests.golden import inputs as gi
+
+    inp = gi.decode_inputs(DECODE_B, seed=0)
+    args = (inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+            inp["scale"])
+    oracle.decode(*args, threads=threads)  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.decode(*args, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    per = el / n
+    return {"value": DECODE_STATE_BYTES / per / 1e9, "unit": "GB/s", "cores": threads or oracle.max_threads(),
+            "kind": "port", "us_per_step": per * 1e6,
+            "sample": f"{n} decode steps at B=64 (CPU oracle, fp32), {el:.1f} s"}
+
+
+def cpu_prefill_baseline(tokens=1024, threads=0):
+    """CPU oracle on the first `tokens` tokens of one sequence: tokens/s (the oracle is linear in T)."""
+    from oracle import oracle
+    from tests.golden import inputs as gi
+
+    inp = gi.prefill_inputs([tokens], seed=0, with_state=True)
+    t0 = time.perf_counter()
+    oracle.prefill(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+                   inp["cu_seqlens"], inp["scale"], threads=threads)
+    el = time.perf_counter() - t0
+    return {"value": tokens / el, "unit": "tokens/s", "cores": threads or oracle.max_threads(), "kind": "port",
+            "sample": f"one {tokens}-token sequence of the 8K workload (CPU oracle), {el:.2f} s; "
+                      f"the sequential oracle's cost is linear in tokens"}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_decode_baseline(budget_s=0.0, threads=threads)
+    times = []
+    from tests.golden import inputs as gi
+
+    inp = gi.decode_inputs(DECODE_B, seed=0)
+    a = (inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"])
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.decode(*a, threads=threads)
+        times.append(time.perf_counter() - t0)
+    per = sum(times) / len(times)
+    val = DECODE_STATE_BYTES / per / 1e9
+    line = {
+        "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode B=64 (qk4_v8_d128, k-last fp32 state), one step", "global_batch": DECODE_B,
+                   "seq_len": 1, "parallelism": "none (rank 0 only, host cores)"},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full decode steps at B=64 of the C restatement of "
+                                   f"reference/gdn_decode_ref.py, {threads} threads"},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local_rank = env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import gdn
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    hbm_peak, tc_peak, peak_src = load_peaks()
+    gen = torch.Generator(device=dev).manual_seed(rank)
+
+    def randn(shape, std=1.0, dtype=torch.float32):
+        return (torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * std).to(dtype)
+
+    def l2n(x):
+        return (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+
+    # ---------------- decode B=64 ----------------
+    B = DECODE_B
+    q = l2n(randn((B, 1, H, D)))
+    k = l2n(randn((B, 1, H, D)))
+    v = randn((B, 1, HV, D), dtype=torch.bfloat16)
+    a = randn((B, 1, HV), dtype=torch.bfloat16)
+    b = randn((B, 1, HV), dtype=torch.bfloat16)
+    A_log = torch.rand(HV, generator=gen, device=dev) * math.log(16.0)
+    dt_bias = randn((HV,), 0.1)
+    scale = 1.0 / math.sqrt(D)
+    states = [randn((B, HV, D, D), 0.02) for _ in range(N_STATE_BUFS)]
+    out = torch.empty((B, 1, HV, D), dtype=torch.bfloat16, device=dev)
+
+    def decode_step(i):
+        st = states[i % N_STATE_BUFS]
+        gdn.decode.kernel(q, k, v, st, A_log, a, dt_bias, b, scale, out, st)
+
+    # CUDA graph of N_STATE_BUFS launches (one per buffer)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(N_STATE_BUFS):
+            decode_step(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(N_STATE_BUFS):
+            decode_step(i)
+    reps = max(1, args.steps // N_STATE_BUFS)
+    steps = reps * N_STATE_BUFS
+    for _ in range(max(1, args.warmup // N_STATE_BUFS + 1)):
+        graph.replay()
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        ev0.record()
+        for _ in range(reps):
+            graph.replay()
+        ev1.record()
+        barrier()
+    dec_ms = ev0.elapsed_time(ev1) / steps
+    dec_ms = max_over_ranks(dec_ms)
+    clock_summary = clocks.summary()
+
+    # eager launches (Python + ctypes path, no graph)
+    barrier()
+    ev0.record()
+    for i in range(steps):
+        decode_step(i)
+    ev1.record()
+    barrier()
+    dec_eager_ms = max_over_ranks(ev0.elapsed_time(ev1) / steps)
+
+    # ---------------- prefill 8K ----------------
+    T = PREFILL_T
+    pq = l2n(randn((T, H, D)))
+    pk = l2n(randn((T, H, D)))
+    pv = randn((T, HV, D), dtype=torch.bfloat16)
+    pa = randn((T, HV), dtype=torch.bfloat16)
+    pb = randn((T, HV), dtype=torch.bfloat16)
+    ph0 = randn((1, HV, D, D), 0.02)
+    cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    pout = torch.empty((T, HV, D), dtype=torch.bfloat16, device=dev)
+    pns = torch.empty((1, HV, D, D), dtype=torch.float32, device=dev)
+    ws = torch.empty(gdn.prefill.workspace_bytes(1, T), dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    from gdn import prefill as pmod
+
+    def prefill_step():
+        pmod._launch(pq, pk, pv, ph0, A_log, pa, dt_bias, pb, cu, scale, pout, pns, workspace=ws)
+
+    for _ in range(args.warmup):
+        prefill_step()
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.prefill_steps)]
+    for e0, e1 in evs:
+        flush.fill_(1)
+        e0.record()
+        prefill_step()
+        e1.record()
+    barrier()
+    pre_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / len(evs)
+    pre_ms = max_over_ranks(pre_ms)
+
+    # ---------------- e2e through the public API with pinned host buffers ----------------
+    e2e = None
+    pre_e2e = None
+    if not args.no_e2e:
+        hq_, hk_, hv_, ha_, hb_ = (t.cpu().pin_memory() for t in (q, k, v, a, b))
+        hst = states[0].cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        hns = torch.empty(hst.shape, dtype=torch.float32).pin_memory()
+        d_in = [torch.empty_like(t, device=dev) for t in (hq_, hk_, hv_, ha_, hb_, hst)]
+        h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, ha_, hb_, hst))
+        d2h = hout.numel() * hout.element_size() + hns.numel() * 4
+        n_e2e = max(3, min(20, args.steps // 10))
+
+        def e2e_step():
+            for dst, src in zip(d_in, (hq_, hk_, hv_, ha_, hb_, hst)):
+                dst.copy_(src, non_blocking=True)
+            gdn.decode.kernel(d_in[0], d_in[1], d_in[2], d_in[5], A_log, d_in[3], dt_bias, d_in[4], scale, out,
+                              d_in[5])
+            hout.copy_(out, non_blocking=True)
+            hns.copy_(d_in[5], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        ev0.record()
+        for _ in range(n_e2e):
+            e2e_step()
+        ev1.record()
+        barrier()
+        e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / n_e2e)
+        e2e = {"value": round(world * DECODE_STATE_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+        hp = [t.cpu().pin_memory() for t in (pq, pk, pv, pa, pb, ph0)]
+        dp = [torch.empty_like(t, device=dev) for t in hp]
+        hpo = torch.empty(pout.shape, dtype=pout.dtype).pin_memory()
+        hpn = torch.empty(pns.shape, dtype=torch.float32).pin_memory()
+        hcu = torch.tensor([0, T], dtype=torch.int32).pin_memory()
+        dcu = torch.empty_like(hcu, device=dev)
+        ph2d = sum(t.numel() * t.element_size() for t in hp) + hcu.numel() * 4
+        pd2h = hpo.numel() * 2 + hpn.numel() * 4
+
+        def pre_e2e_step():
+            for dst, src in zip(dp, hp):
+                dst.copy_(src, non_blocking=True)
+            dcu.copy_(hcu, non_blocking=True)
+            gdn.prefill.kernel(dp[0], dp[1], dp[2], dp[5], A_log, dp[3], dt_bias, dp[4], dcu, scale, pout, pns)
+            hpo.copy_(pout, non_blocking=True)
+            hpn.copy_(pns, non_blocking=True)
+
+        for _ in range(2):
+            pre_e2e_step()
+        barrier()
+        ev0.record()
+        for _ in range(n_e2e):
+            pre_e2e_step()
+        ev1.record()
+        barrier()
+        pe_ms = max_over_ranks(ev0.elapsed_time(ev1) / n_e2e)
+        pre_e2e = {"value": round(world * T / (pe_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(pe_ms, 4),
+                   "h2d_bytes_per_step": ph2d, "d2h_bytes_per_step": pd2h}
+
+    # ---------------- report ----------------
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_decode_baseline(budget_s=args.cpu_budget)
+        cpu_pre = cpu_prefill_baseline(1024)
+    dec_us = dec_ms * 1e3
+    value = world * DECODE_STATE_BYTES / (dec_ms * 1e-3) / 1e9
+    achieved = DECODE_ALG_BYTES / (dec_ms * 1e-3) / 1e9
+    pre_bytes = T * PREFILL_ALG_BYTES_PER_TOKEN + 2 * STATE_BYTES_PER_ELEM
+    pre_flops = T * PREFILL_FLOPS_PER_TOKEN
+    pre_bound_s = max(pre_bytes / (hbm_peak * 1e9), pre_flops / (tc_peak * 1e12))
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dec_ms, 6),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "decode B=64 per GPU (qk4_v8_d128, k-last fp32 state, in place), one step",
+                   "global_batch": DECODE_B * world, "seq_len": 1, "parallelism": f"dp{world} (independent shards)",
+                   "l2": f"{N_STATE_BUFS} rotating state buffers ({N_STATE_BUFS * 32} MiB > 126 MB L2)",
+                   "timing": "CUDA graph replays, CUDA events, max over ranks"},
+        "decode_us_per_step": round(dec_us, 3),
+        "decode_eager_us_per_step": round(dec_eager_ms * 1e3, 3),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": NCU_TRAFFIC["decode"],
+                     "kernel": "gdn_decode_kernel", "peak_source": peak_src},
+        "prefill_8k": {
+            "tokens_per_s": round(world * T / (pre_ms * 1e-3), 1), "ms_per_step": round(pre_ms, 5),
+            "config": "one 8192-token sequence per GPU, cu_seqlens int32, initial state N(0,0.02); L2 flushed",
+            "roofline": {"bound": "max(hbm, tensor)", "achieved_frac": round(pre_bound_s / (pre_ms * 1e-3), 5),
+                         "bound_us": round(pre_bound_s * 1e6, 3), "alg_bytes": pre_bytes, "alg_flops": pre_flops,
+                         "traffic": NCU_TRAFFIC["prefill_scan"], "peak_source": peak_src},
+            "e2e": pre_e2e,
+        },
+        "e2e": e2e,
+        "gpu_launches": steps,
+        "clocks": clock_summary,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+        line["prefill_8k"]["cpu_baseline"] = cpu_pre
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

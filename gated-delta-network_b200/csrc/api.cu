@@ -1,0 +1,151 @@
+// api.cu -- extern "C" entry points declared in include/gdn_b200.h.
+//
+// Host-side validation mirrors the reference's shape asserts
+// (reference/gdn_decode_ref.py:32-36, reference/gdn_prefill_ref.py:33-36) and
+// adds the checks the kernels rely on (alignment, workspace size, device).
+// Nothing here synchronises, copies to the host or allocates device memory.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"
+#include "common.cuh"
+
+#include "kernels.cuh"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+// 0 = unknown, 1 = sm_100 family, 2 = other.  Benign race: every writer stores the same value.
+int g_dev_ok[kMaxDevices];
+
+int check_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxDevices) return GDN_ERR_DEVICE;
+    if (g_dev_ok[dev] == 0) {
+        int major = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return GDN_ERR_CUDA;
+        g_dev_ok[dev] = (major == 10) ? 1 : 2;
+    }
+    return g_dev_ok[dev] == 1 ? GDN_OK : GDN_ERR_DEVICE;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool shape_ok(int H, int HV, int K, int V) {
+    return H == GDN_NUM_QK_HEADS && HV == GDN_NUM_V_HEADS && K == GDN_HEAD_DIM && V == GDN_HEAD_DIM;
+}
+
+int decode_variant(int B, unsigned flags) {
+    const unsigned forced = (flags >> 8) & 0xffu;  // tuning override: variant + 1
+    if (forced) return (int)forced - 1;
+    // 8 heads per batch element; keep >= ~2 CTAs per SM in flight.
+    if (B <= 8) return 2;
+    if (B <= 32) return 0;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                   const void* a, const float* dt_bias, const void* b, float scale, void* out, float* new_state,
+                   int B, int H, int HV, int K, int V, void* stream, unsigned flags) {
+    if (!shape_ok(H, HV, K, V)) return GDN_ERR_SHAPE;
+    if (B < 0) return GDN_ERR_SIZE;
+    if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !out || !new_state) return GDN_ERR_NULL;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(new_state) ||
+        (state && !aligned16(state)))
+        return GDN_ERR_ALIGN;
+    if (B == 0) return GDN_OK;
+    int rc = check_device();
+    if (rc != GDN_OK) return rc;
+    gdn::DecodeArgs p;
+    p.q = static_cast<const uint16_t*>(q);
+    p.k = static_cast<const uint16_t*>(k);
+    p.v = static_cast<const uint16_t*>(v);
+    p.state = state;
+    p.A_log = A_log;
+    p.a = static_cast<const uint16_t*>(a);
+    p.dt_bias = dt_bias;
+    p.b = static_cast<const uint16_t*>(b);
+    p.scale = scale;
+    p.out = static_cast<uint16_t*>(out);
+    p.new_state = new_state;
+    p.B = B;
+    if (gdn::launch_decode(p, decode_variant(B, flags), static_cast<cudaStream_t>(stream)) != 0) return GDN_ERR_SIZE;
+    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV, int K, int V) {
+    if (!shape_ok(H, HV, K, V) || N < 0 || T < 0) return 0;
+    size_t ow, ou, oa, og;
+    return gdn::prefill_workspace_layout(T, &ow, &ou, &oa, &og);
+}
+
+int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                    const void* a, const float* dt_bias, const void* b, const void* cu_seqlens, int cu_is_int64,
+                    int N, int T, float scale, void* out, float* new_state, void* workspace, size_t workspace_bytes,
+                    int H, int HV, int K, int V, void* stream, unsigned flags) {
+    (void)flags;
+    if (!shape_ok(H, HV, K, V)) return GDN_ERR_SHAPE;
+    if (N < 0 || T < 0) return GDN_ERR_SIZE;
+    if (N == 0) return GDN_OK;
+    if (!cu_seqlens || !new_state || !A_log || !dt_bias) return GDN_ERR_NULL;
+    if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL;
+    if ((T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))) || !aligned16(new_state) ||
+        (state && !aligned16(state)))
+        return GDN_ERR_ALIGN;
+    if (cu_is_int64 != 0 && cu_is_int64 != 1) return GDN_ERR_SIZE;
+    size_t ow, ou, oa, og;
+    const size_t need = gdn::prefill_workspace_layout(T, &ow, &ou, &oa, &og);
+    if (T > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
+        return GDN_ERR_WORKSPACE;
+    int rc = check_device();
+    if (rc != GDN_OK) return rc;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    gdn::PrefillArgs p;
+    p.q = static_cast<const uint16_t*>(q);
+    p.k = static_cast<const uint16_t*>(k);
+    p.v = static_cast<const uint16_t*>(v);
+    p.state = state;
+    p.A_log = A_log;
+    p.a = static_cast<const uint16_t*>(a);
+    p.dt_bias = dt_bias;
+    p.b = static_cast<const uint16_t*>(b);
+    p.cu = cu_seqlens;
+    p.cu64 = cu_is_int64;
+    p.N = N;
+    p.T = T;
+    p.scale = scale;
+    p.out = static_cast<uint16_t*>(out);
+    p.new_state = new_state;
+    p.w = T > 0 ? reinterpret_cast<uint16_t*>(ws + ow) : nullptr;
+    p.u = T > 0 ? reinterpret_cast<float*>(ws + ou) : nullptr;
+    p.aqk = T > 0 ? reinterpret_cast<uint16_t*>(ws + oa) : nullptr;
+    p.g = T > 0 ? reinterpret_cast<float*>(ws + og) : nullptr;
+    const unsigned forced_bv = (flags >> 8) & 0xffu;
+    const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N);
+    if (bv != 16 && bv != 32) return GDN_ERR_SIZE;
+    if (gdn::launch_prefill(p, bv, static_cast<cudaStream_t>(stream)) != 0) return GDN_ERR_CUDA;
+    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+const char* gdn_status_string(int status) {
+    switch (status) {
+        case GDN_OK: return "ok";
+        case GDN_ERR_NULL: return "a required pointer is NULL";
+        case GDN_ERR_SHAPE: return "unsupported shape (need H=4, HV=8, K=V=128)";
+        case GDN_ERR_ALIGN: return "a tensor pointer is not 16-byte aligned";
+        case GDN_ERR_SIZE: return "invalid size or option";
+        case GDN_ERR_WORKSPACE: return "workspace missing, misaligned (256 B) or too small";
+        case GDN_ERR_CUDA: return "CUDA launch failed";
+        case GDN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+        default: return "unknown status";
+    }
+}
+
+int gdn_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,102 @@
+// common.cuh -- shared device helpers for the Gated DeltaNet sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int kH = 4;       // q/k heads
+constexpr int kHV = 8;      // v heads (GVA: v-head hv reads q/k head hv / 2)
+constexpr int kD = 128;     // head dim K == V
+constexpr int kChunk = 64;  // prefill chunk length
+
+__device__ __forceinline__ float bf2f(uint16_t x) { return __uint_as_float(((uint32_t)x) << 16); }
+
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    __nv_bfloat16 h = __float2bfloat16_rn(f);
+    return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// Two floats -> packed bf16x2 (lo in the low half), round to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// softplus with PyTorch's threshold (beta = 1, threshold = 20), as in
+// reference/gdn_decode_ref.py:43 (F.softplus) and triton/kernel.py:50.
+__device__ __forceinline__ float softplus_t20(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// Log-space decay g = -exp(A_log) * softplus(a + dt_bias) and beta = sigmoid(b)
+// (reference/gdn_decode_ref.py:42-44).
+__device__ __forceinline__ float log_decay(float a, float A_log, float dt_bias) {
+    return -expf(A_log) * softplus_t20(a + dt_bias);
+}
+__device__ __forceinline__ float sigmoidf_(float b) { return 1.0f / (1.0f + expf(-b)); }
+
+// ---- global memory access with cache hints -------------------------------------------------
+// State is touched exactly once per call: stream it (evict-first) so q/k/v stay cached.
+__device__ __forceinline__ float4 ld_stream_f4(const float* p) {
+    float4 r;
+    asm volatile("ld.global.cs.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ void st_stream_f4(float* p, float4 v) {
+    asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ uint2 ld_nc_u2(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+
+// ---- cp.async (16-byte global -> shared) ---------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+    // src-size 0 zero-fills the 16 bytes when pred is false (rows past the chunk end).
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+                 "r"(pred ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---- warp-level bf16 tensor-core fragments (m16n8k16, fp32 accumulate) ---------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Swizzled offset (in elements) inside a [rows][128] bf16 tile: the 16-byte
+// chunk index is XORed with the row's low 3 bits so that ldmatrix row reads
+// of 8 consecutive rows hit 8 different bank groups.
+__device__ __forceinline__ int swz128(int row, int col) {
+    return row * 128 + ((((col >> 3) ^ row) & 7) | ((col >> 3) & ~7)) * 8 + (col & 7);
+}
+// Same for [rows][64] bf16 tiles (8 chunks of 16 bytes per row).
+__device__ __forceinline__ int swz64(int row, int col) { return row * 64 + (((col >> 3) ^ row) & 7) * 8 + (col & 7); }
+
+}  // namespace gdn

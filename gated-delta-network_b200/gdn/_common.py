@@ -1,0 +1,43 @@
+"""Argument normalisation shared by the decode and prefill entry points."""
+from __future__ import annotations
+
+import math
+
+import torch
+
+NUM_QK_HEADS = 4
+NUM_V_HEADS = 8
+HEAD_DIM = 128
+
+
+def resolve_scale(scale) -> float:
+    """None / 0 -> 1/sqrt(128) (reference/gdn_decode_ref.py:38-39); 0-d tensors -> .item()
+    (solutions/gdn_decode_qk4_v8_d128_k_last/solution/triton/kernel.py:92-93)."""
+    if isinstance(scale, torch.Tensor):
+        scale = scale.item()
+    if scale is None or float(scale) == 0.0:
+        return 1.0 / math.sqrt(HEAD_DIM)
+    return float(scale)
+
+
+def cuda_device(t: torch.Tensor, name: str) -> torch.device:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); there is no CPU path")
+    return t.device
+
+
+def as_dev(t: torch.Tensor, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """Contiguous tensor of `dtype` on `device` (copies only when needed)."""
+    if t.device != device or t.dtype != dtype:
+        t = t.to(device=device, dtype=dtype)
+    return t.contiguous()
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream

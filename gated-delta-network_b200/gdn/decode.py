@@ -1,0 +1,75 @@
+"""Gated DeltaNet decode step on B200 (single token per sequence).
+
+Drop-in for reference/gdn_decode_ref.py:12 (``run``) and for the
+destination-passing ``kernel`` of
+solutions/gdn_decode_qk4_v8_d128_k_last/solution/triton/kernel.py:85.
+Both call ``gdn_decode_fwd`` of libgdn_b200.so on the current CUDA stream;
+nothing synchronises the host unless ``scale`` is a CUDA tensor (``.item()``,
+as in the reference).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._common import HEAD_DIM, NUM_QK_HEADS, NUM_V_HEADS, as_dev, cuda_device, ptr, resolve_scale, stream_handle
+
+
+def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, flags=0):
+    dev = cuda_device(q, "q")
+    B, T, Hq, K = q.shape
+    Hk = k.shape[2]
+    HV, V = v.shape[2], v.shape[3]
+    # Same shape contract as the reference oracle (reference/gdn_decode_ref.py:32-36).
+    assert Hq == NUM_QK_HEADS
+    assert Hk == NUM_QK_HEADS
+    assert HV == NUM_V_HEADS
+    assert K == HEAD_DIM and V == HEAD_DIM
+    assert T == 1
+    s = resolve_scale(scale)
+    q_ = as_dev(q, torch.bfloat16, dev)
+    k_ = as_dev(k, torch.bfloat16, dev)
+    v_ = as_dev(v, torch.bfloat16, dev)
+    a_ = as_dev(a, torch.bfloat16, dev)
+    b_ = as_dev(b, torch.bfloat16, dev)
+    A_ = as_dev(A_log, torch.float32, dev)
+    d_ = as_dev(dt_bias, torch.float32, dev)
+    if tuple(a_.shape[-1:]) != (HV,) or a_.numel() != B * HV or b_.numel() != B * HV:
+        raise ValueError("a and b must hold [B, 1, 8] gate inputs")
+    if A_.numel() != HV or d_.numel() != HV:
+        raise ValueError("A_log and dt_bias must hold 8 values")
+    st = None
+    if state is not None:
+        if tuple(state.shape) != (B, HV, V, K):
+            raise ValueError(f"state must be [B, 8, 128, 128], got {tuple(state.shape)}")
+        st = as_dev(state, torch.float32, dev)
+    for name, t, shape, dt in (("output", output, (B, HV * V), torch.bfloat16),
+                               ("new_state", new_state, (B, HV * V * K), torch.float32)):
+        if t.device != dev or t.dtype != dt or not t.is_contiguous() or t.numel() != shape[0] * shape[1]:
+            raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor with {shape[0] * shape[1]} elements")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.gdn_decode_fwd(ptr(q_), ptr(k_), ptr(v_), ptr(st), ptr(A_), ptr(a_), ptr(d_), ptr(b_), s,
+                                ptr(output), ptr(new_state), B, Hq, HV, K, V, stream_handle(dev), flags)
+    _lib.check("gdn_decode_fwd", rc)
+
+
+@torch.no_grad()
+def run(q, k, v, state, A_log, a, dt_bias, b, scale):
+    """One decode step.  Returns ``(output [B,1,8,128] bf16, new_state [B,8,128,128] fp32)``.
+
+    q, k [B,1,4,128] bf16; v [B,1,8,128] bf16; state [B,8,128,128] fp32 (k-last) or None (zeros);
+    A_log, dt_bias [8] fp32; a, b [B,1,8] bf16; scale float, 0-d tensor, or None/0 (1/sqrt(128)).
+    """
+    B = q.shape[0]
+    dev = cuda_device(q, "q")
+    output = torch.empty((B, 1, NUM_V_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    new_state = torch.empty((B, NUM_V_HEADS, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
+    _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+    return output, new_state
+
+
+@torch.no_grad()
+def kernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+    """Destination-passing decode: writes ``output`` and ``new_state`` (which may be ``state`` itself)."""
+    _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)

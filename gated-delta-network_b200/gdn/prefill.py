@@ -1,0 +1,99 @@
+"""Gated DeltaNet varlen chunked prefill on B200.
+
+Drop-in for reference/gdn_prefill_ref.py:12 (``run``) and for the
+destination-passing ``kernel`` of
+solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/fla_kernels.py:1049.
+``cu_seqlens`` (int32 or int64) is read on the device only; unlike the
+reference (fla_kernels.py:963, ``cu_seqlens.tolist()``) no call copies it to
+the host, so a call can be captured into a CUDA graph.  The intermediate
+workspace (w, u, Aqk, G: about 7.2 KB per token) comes from the torch caching
+allocator, or from the caller through ``workspace=``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._common import HEAD_DIM, NUM_QK_HEADS, NUM_V_HEADS, as_dev, cuda_device, ptr, resolve_scale, stream_handle
+
+
+def workspace_bytes(num_seqs: int, total_tokens: int) -> int:
+    return int(_lib.load().gdn_prefill_workspace_bytes(int(num_seqs), int(total_tokens), NUM_QK_HEADS,
+                                                       NUM_V_HEADS, HEAD_DIM, HEAD_DIM))
+
+
+def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, workspace=None, flags=0):
+    dev = cuda_device(q, "q")
+    T, Hq, K = q.shape
+    Hk = k.shape[1]
+    HV, V = v.shape[1], v.shape[2]
+    N = cu_seqlens.shape[0] - 1
+    # Same shape contract as the reference oracle (reference/gdn_prefill_ref.py:33-36).
+    assert Hq == NUM_QK_HEADS
+    assert Hk == NUM_QK_HEADS
+    assert HV == NUM_V_HEADS
+    assert K == HEAD_DIM and V == HEAD_DIM
+    if N < 0:
+        raise ValueError("cu_seqlens must hold at least one element")
+    s = resolve_scale(scale)
+    if cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise ValueError("cu_seqlens must be int32 or int64")
+    cu = cu_seqlens if cu_seqlens.device == dev else cu_seqlens.to(dev)
+    cu = cu.contiguous()
+    q_ = as_dev(q, torch.bfloat16, dev)
+    k_ = as_dev(k, torch.bfloat16, dev)
+    v_ = as_dev(v, torch.bfloat16, dev)
+    a_ = as_dev(a, torch.bfloat16, dev)
+    b_ = as_dev(b, torch.bfloat16, dev)
+    A_ = as_dev(A_log, torch.float32, dev)
+    d_ = as_dev(dt_bias, torch.float32, dev)
+    if a_.numel() != T * HV or b_.numel() != T * HV:
+        raise ValueError("a and b must hold [T, 8] gate inputs")
+    if A_.numel() != HV or d_.numel() != HV:
+        raise ValueError("A_log and dt_bias must hold 8 values")
+    st = None
+    if state is not None:
+        if tuple(state.shape) != (N, HV, V, K):
+            raise ValueError(f"state must be [N, 8, 128, 128], got {tuple(state.shape)}")
+        st = as_dev(state, torch.float32, dev)
+    for name, t, n, dt in (("output", output, T * HV * V, torch.bfloat16),
+                           ("new_state", new_state, N * HV * V * K, torch.float32)):
+        if t.device != dev or t.dtype != dt or not t.is_contiguous() or t.numel() != n:
+            raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor with {n} elements")
+    lib = _lib.load()
+    need = workspace_bytes(N, T)
+    if workspace is None:
+        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    else:
+        ws = workspace
+        if ws.device != dev or ws.numel() * ws.element_size() < need:
+            raise ValueError(f"workspace must be a CUDA buffer of at least {need} bytes")
+    with torch.cuda.device(dev):
+        rc = lib.gdn_prefill_fwd(ptr(q_), ptr(k_), ptr(v_), ptr(st), ptr(A_), ptr(a_), ptr(d_), ptr(b_), ptr(cu),
+                                 1 if cu.dtype == torch.int64 else 0, N, T, s, ptr(output), ptr(new_state),
+                                 ptr(ws), need, Hq, HV, K, V, stream_handle(dev), flags)
+    _lib.check("gdn_prefill_fwd", rc)
+
+
+@torch.no_grad()
+def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+    """Varlen prefill.  Returns ``(output [T,8,128] bf16, new_state [N,8,128,128] fp32)``.
+
+    q, k [T,4,128] bf16; v [T,8,128] bf16; state [N,8,128,128] fp32 or None; a, b [T,8] bf16;
+    cu_seqlens [N+1] int32/int64; scale float, 0-d tensor, or None/0 (1/sqrt(128)).
+    Tokens outside every sequence keep a zero output, and a zero-length sequence
+    gets an all-zero final state, as in the reference oracle.
+    """
+    dev = cuda_device(q, "q")
+    T = q.shape[0]
+    N = cu_seqlens.shape[0] - 1
+    output = torch.empty((T, NUM_V_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    new_state = torch.empty((max(N, 0), NUM_V_HEADS, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
+    _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+    return output, new_state
+
+
+@torch.no_grad()
+def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):
+    """Destination-passing prefill: writes ``output`` and ``new_state`` (which may be ``state``)."""
+    _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)

@@ -1,0 +1,121 @@
+/*
+ * gdn_b200.h -- C ABI of the B200-native Gated DeltaNet operator pair
+ * (decode step and varlen chunked prefill), shape family qk4_v8_d128,
+ * k-last fp32 recurrent state [*, HV, V, K].
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as void*; no framework types cross this boundary.  All launches are
+ * asynchronous on the given stream; no entry point synchronises the device,
+ * copies device data to the host or allocates device memory, so every call
+ * can be captured into a CUDA graph.
+ *
+ * Element types:
+ *   bf16  = 16-bit brain float stored as uint16_t bits (torch.bfloat16)
+ *   f32   = IEEE float
+ * Return value: GDN_OK (0) or one of the GDN_ERR_* codes below; a non-zero
+ * return means nothing was launched (except GDN_ERR_CUDA, which reports a
+ * launch failure from the CUDA runtime).
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum gdn_status {
+    GDN_OK = 0,
+    GDN_ERR_NULL = 1,      /* a required pointer is NULL                          */
+    GDN_ERR_SHAPE = 2,     /* head counts / head size other than 4, 8, 128, 128    */
+    GDN_ERR_ALIGN = 3,     /* a pointer is not 16-byte aligned                     */
+    GDN_ERR_SIZE = 4,      /* negative or inconsistent batch / token / seq counts  */
+    GDN_ERR_WORKSPACE = 5, /* workspace missing, misaligned or too small           */
+    GDN_ERR_CUDA = 6,      /* the CUDA runtime rejected the launch                 */
+    GDN_ERR_DEVICE = 7     /* current device is not sm_100 (B200)                 */
+};
+
+/* Flags (bitwise OR) accepted by the entry points. */
+#define GDN_FLAG_NONE 0u
+
+/* Fixed shape family (the reference asserts exactly these:
+ * reference/gdn_decode_ref.py:32-36, reference/gdn_prefill_ref.py:33-36). */
+#define GDN_NUM_QK_HEADS 4
+#define GDN_NUM_V_HEADS 8
+#define GDN_HEAD_DIM 128
+#define GDN_CHUNK 64
+
+/*
+ * One decode step for a batch of B sequences.
+ *
+ * Replaces the destination-passing entry
+ *   kernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+ * of solutions/gdn_decode_qk4_v8_d128_k_last/solution/triton/kernel.py:85
+ * (and its CUDA twin, solutions/gdn_decode_qk4_v8_d128_k_last/solution/cuda/binding.py:195),
+ * with the semantics of reference/gdn_decode_ref.py:12-83 (run).
+ *
+ *   q, k      [B, H=4, K=128]        bf16   (the reference's [B,1,4,128])
+ *   v         [B, HV=8, V=128]       bf16
+ *   state     [B, HV, V, K]          f32    k-last; NULL means an all-zero state
+ *   A_log     [HV]                   f32
+ *   a, b      [B, HV]                bf16
+ *   dt_bias   [HV]                   f32
+ *   scale     softmax-free output scale (the caller resolves None/0 to 1/sqrt(K))
+ *   out       [B, HV, V]             bf16   (written)
+ *   new_state [B, HV, V, K]          f32    (written; may alias `state`)
+ *   H, HV, K, V must be 4, 8, 128, 128.  B may be 0 (no launch).
+ * Pointers to q, k, v, state, out, new_state must be 16-byte aligned.
+ */
+int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                   const void* a, const float* dt_bias, const void* b, float scale, void* out, float* new_state,
+                   int B, int H, int HV, int K, int V, void* stream, unsigned flags);
+
+/*
+ * Workspace bytes gdn_prefill_fwd needs for T packed tokens and N sequences.
+ * Replaces the module-level buffer cache of
+ * solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/fla_kernels.py:950-957,987-1037
+ * (the caller owns the memory; the library keeps no global device state).
+ */
+size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV, int K, int V);
+
+/*
+ * Varlen chunked prefill (chunk = 64 tokens) over N packed sequences.
+ *
+ * Replaces the destination-passing entry
+ *   kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+ * of solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/fla_kernels.py:1049
+ * (and the legacy FLA wrapper, solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/kernel.py:61-104),
+ * with the semantics of reference/gdn_prefill_ref.py:12-91 (run).
+ *
+ *   q, k        [T, H=4, K=128]      bf16
+ *   v           [T, HV=8, V=128]     bf16
+ *   state       [N, HV, V, K]        f32    initial state, k-last; NULL means zeros
+ *   A_log       [HV] f32; a, b [T, HV] bf16; dt_bias [HV] f32
+ *   cu_seqlens  [N+1]                int32 (cu_is_int64 = 0) or int64 (cu_is_int64 = 1),
+ *                                    device memory; read on the device only (no host copy)
+ *   out         [T, HV, V]           bf16   (written for every token covered by a sequence)
+ *   new_state   [N, HV, V, K]        f32    final state; a zero-length sequence gets all zeros
+ *                                    (reference/gdn_prefill_ref.py:52-54, 61-62); may alias `state`
+ *   workspace   >= gdn_prefill_workspace_bytes(N, T, ...) bytes of device memory, 256-byte aligned;
+ *               no contents are carried between calls.
+ * Sequence bounds are clamped to [0, T] on the device, so malformed cu_seqlens
+ * cannot make the kernels read or write outside the buffers.
+ */
+int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                    const void* a, const float* dt_bias, const void* b, const void* cu_seqlens, int cu_is_int64,
+                    int N, int T, float scale, void* out, float* new_state, void* workspace, size_t workspace_bytes,
+                    int H, int HV, int K, int V, void* stream, unsigned flags);
+
+/* Human-readable name of a status code (static storage). */
+const char* gdn_status_string(int status);
+
+/* Library version, major*10000 + minor*100 + patch. */
+int gdn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

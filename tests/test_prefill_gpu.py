@@ -1,0 +1,190 @@
+"""Prefill parity on the GPU: the CUDA path (through the C ABI) against the CPU oracle
+and the reference's golden outputs.  Cases follow the reference's own prefill tests
+(in-chunk, multi-chunk, ragged tails, multi-sequence, initial state) plus the
+benchmark configurations at full size."""
+import numpy as np
+import pytest
+import torch
+
+import gdn
+from oracle import oracle
+from tests import util
+from tests.golden import check, inputs as gi
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle(inp):
+    return oracle.prefill(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"],
+                          inp["b"], inp["cu_seqlens"], inp["scale"])
+
+
+def _run_and_check(inp, cu_dtype=torch.int32):
+    out, ns = gdn.prefill.run(*util.prefill_args(inp, cu_dtype=cu_dtype))
+    torch.cuda.synchronize()
+    ro, rs = _oracle(inp)
+    err = util.check_out(util.bits(out), ro)
+    rel = util.check_state(ns.cpu().numpy(), rs)
+    return err, rel
+
+
+CASES = [
+    ([32], False), ([64], False), ([128], False), ([256], False),
+    ([31], False), ([65], False), ([127], False),
+    ([64, 64], False), ([32, 96], False), ([64, 128], False),
+    ([64], True), ([128], True), ([64, 128], True),
+    ([1], True), ([2, 3, 1, 63, 129], True), ([1000], True),
+]
+
+
+@pytest.mark.parametrize("lens,with_state", CASES, ids=[f"{'-'.join(map(str, l))}{'-h0' if s else ''}"
+                                                         for l, s in CASES])
+def test_prefill_matches_oracle(lens, with_state):
+    inp = gi.prefill_inputs(lens, seed=sum(lens) + 7 * len(lens), with_state=with_state)
+    _run_and_check(inp)
+
+
+@pytest.mark.parametrize("name,fx", check.fixtures("prefill"), ids=[n for n, _ in check.fixtures("prefill")])
+def test_prefill_matches_reference_golden(name, fx):
+    inp = check.regen(fx)
+    out, ns = gdn.prefill.run(*util.prefill_args(inp))
+    torch.cuda.synchronize()
+    check.compare(fx, "out", util.bits(out), atol=util.OUT_ATOL, rtol=util.OUT_RTOL, proj_rtol=1e-2)
+    # state: the bar is rel-L2 1e-3; projections on +-1 vectors bound it the same way
+    check.compare(fx, "state", ns.cpu().numpy(), atol=1e-3, rtol=1e-2, proj_rtol=1e-3)
+
+
+def test_prefill_int64_cu_seqlens():
+    inp = gi.prefill_inputs([70, 33, 129], seed=21)
+    o32, s32 = gdn.prefill.run(*util.prefill_args(inp, cu_dtype=torch.int32))
+    o64, s64 = gdn.prefill.run(*util.prefill_args(inp, cu_dtype=torch.int64))
+    torch.cuda.synchronize()
+    assert torch.equal(o32, o64) and torch.equal(s32, s64)
+
+
+def test_prefill_cpu_cu_seqlens_accepted():
+    inp = gi.prefill_inputs([50, 14], seed=22)
+    args = list(util.prefill_args(inp))
+    ref = gdn.prefill.run(*args)
+    args[8] = args[8].cpu()
+    got = gdn.prefill.run(*args)
+    torch.cuda.synchronize()
+    assert torch.equal(ref[0], got[0]) and torch.equal(ref[1], got[1])
+
+
+def test_prefill_zero_length_sequences():
+    inp = gi.prefill_inputs([40, 0, 70, 0], seed=23)
+    out, ns = gdn.prefill.run(*util.prefill_args(inp))
+    torch.cuda.synchronize()
+    ro, rs = _oracle(inp)
+    util.check_out(util.bits(out), ro)
+    util.check_state(ns.cpu().numpy(), rs)
+    assert torch.count_nonzero(ns[1]) == 0 and torch.count_nonzero(ns[3]) == 0
+
+
+def test_prefill_uncovered_tokens_are_zero():
+    """Tokens outside [cu[0], cu[N]) keep a zero output (the reference zero-initialises output)."""
+    inp = gi.prefill_inputs([100], seed=24)
+    T = 100
+    inp["cu_seqlens"] = np.array([10, 80], np.int32)
+    out, ns = gdn.prefill.run(*util.prefill_args(inp))
+    torch.cuda.synchronize()
+    ro, rs = _oracle(inp)
+    util.check_out(util.bits(out), ro)
+    util.check_state(ns.cpu().numpy(), rs)
+    assert torch.count_nonzero(out[:10]) == 0 and torch.count_nonzero(out[80:]) == 0
+    assert out.shape[0] == T
+
+
+def test_prefill_t1_matches_decode():
+    d = gi.decode_inputs(6, seed=25)
+    q, k, v, st, A_log, a, dt_bias, b, scale = util.decode_args(d)
+    od, sd = gdn.decode.run(q, k, v, st, A_log, a, dt_bias, b, scale)
+    cu = torch.arange(7, dtype=torch.int32, device="cuda")
+    op, sp = gdn.prefill.run(q.view(6, 4, 128), k.view(6, 4, 128), v.view(6, 8, 128), st, A_log, a.view(6, 8),
+                             dt_bias, b.view(6, 8), cu, scale)
+    torch.cuda.synchronize()
+    util.check_out(util.bits(op), util.bits(od.view(6, 8, 128)), atol=1e-3, rtol=1e-2)
+    util.check_state(sp.cpu().numpy(), sd.cpu().numpy(), rel_l2=1e-4)
+
+
+def test_prefill_in_place_state_dps():
+    inp = gi.prefill_inputs([90, 200], seed=26)
+    args = util.prefill_args(inp)
+    ro, rs = gdn.prefill.run(*args)
+    q, k, v, st, A_log, a, dt_bias, b, cu, scale = args
+    out = torch.empty_like(ro)
+    gdn.prefill.kernel(q, k, v, st, A_log, a, dt_bias, b, cu, scale, out, st)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ro) and torch.equal(st, rs)
+
+
+def test_prefill_deterministic_and_bv_variants():
+    from gdn import prefill as pmod
+
+    inp = gi.prefill_inputs([300, 77], seed=27)
+    args = util.prefill_args(inp)
+    o1, s1 = gdn.prefill.run(*args)
+    o2, s2 = gdn.prefill.run(*args)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    for bv in (16, 32):
+        out = torch.empty_like(o1)
+        ns = torch.empty_like(s1)
+        pmod._launch(*args, out, ns, flags=bv << 8)
+        torch.cuda.synchronize()
+        assert torch.equal(out, o1) and torch.equal(ns, s1)
+
+
+def test_prefill_strong_decay_extremes():
+    inp = gi.prefill_inputs([130, 64], seed=28)
+    inp["A_log"] = np.array([np.log(16.0), 0.0, -8.0, np.log(16.0), -20.0, 2.0, 0.5, -1.0], np.float32)
+    rng = np.random.default_rng(5)
+    inp["a"] = gi.to_bf16_bits((rng.standard_normal((194, 8)) * 10).astype(np.float32))
+    _run_and_check(inp)
+
+
+def test_prefill_graph_capture():
+    inp = gi.prefill_inputs([256, 100], seed=29)
+    q, k, v, st, A_log, a, dt_bias, b, cu, scale = util.prefill_args(inp)
+    ro, rs = gdn.prefill.run(q, k, v, st, A_log, a, dt_bias, b, cu, scale)
+    out = torch.empty_like(ro)
+    ns = torch.empty_like(rs)
+    ws = torch.empty(gdn.prefill.workspace_bytes(2, 356), dtype=torch.uint8, device="cuda")
+    from gdn import prefill as pmod
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        pmod._launch(q, k, v, st, A_log, a, dt_bias, b, cu, scale, out, ns, workspace=ws)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        pmod._launch(q, k, v, st, A_log, a, dt_bias, b, cu, scale, out, ns, workspace=ws)
+    out.zero_()
+    ns.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ro) and torch.equal(ns, rs)
+
+
+# ---- benchmark configurations at full size ------------------------------------------------
+
+def test_prefill_config2_t1024():
+    inp = gi.prefill_inputs([1024], seed=0, with_state=False)
+    _run_and_check(inp)
+
+
+def test_prefill_config3_varlen_16_seqs():
+    lens = gi.varlen_lengths(16, 6, 8192, 32768, seed=0)
+    inp = gi.prefill_inputs(lens, seed=0, with_state=True)
+    _run_and_check(inp)
+
+
+def test_prefill_8k_single_sequence():
+    inp = gi.prefill_inputs([8192], seed=0, with_state=True)
+    _run_and_check(inp)
+
+
+def test_prefill_packed_8x1024():
+    inp = gi.prefill_inputs([1024] * 8, seed=1, with_state=True)
+    _run_and_check(inp)
