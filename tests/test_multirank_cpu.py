@@ -1,0 +1,101 @@
+"""Multi-process (gloo, world_size 2) checks of the sharded path on CPU: every rank runs the
+oracle on its own shard, the shards reassemble into the single-process result, and the
+timing reduction used by bench.py (MAX over ranks) behaves.  No GPU involved."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gdn.shard import batch_shard, seq_shard
+
+
+def test_batch_shard_covers_everything():
+    for B in (0, 1, 7, 64, 512):
+        for world in (1, 2, 3, 8):
+            spans = [batch_shard(B, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == B
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1
+
+
+def test_seq_shard_rebases_and_covers():
+    cu = [0, 4096 * 1, 4096 * 2, 4096 * 3, 4096 * 4]
+    parts = [seq_shard(cu, 2, r) for r in range(2)]
+    assert parts[0][:4] == (0, 2, 0, 8192) and parts[1][:4] == (2, 4, 8192, 16384)
+    assert parts[1][4] == [0, 4096, 8192]
+    cu2 = [0, 5, 5, 100, 130, 131]
+    for world in (1, 2, 3, 4):
+        ps = [seq_shard(cu2, world, r) for r in range(world)]
+        assert ps[0][0] == 0 and ps[-1][1] == 5
+        assert all(ps[i][1] == ps[i + 1][0] for i in range(world - 1))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import torch
+
+        from oracle import oracle
+        from tests.golden import inputs as gi
+
+        # decode: shard a batch of 6
+        d = gi.decode_inputs(6, seed=3)
+        s0, s1 = batch_shard(6, world, rank)
+        o, st = oracle.decode(*(d[x][s0:s1] for x in ("q", "k", "v", "state")), d["A_log"], d["a"][s0:s1],
+                              d["dt_bias"], d["b"][s0:s1], d["scale"], threads=1)
+        dec = [None] * world
+        dist.all_gather_object(dec, (o, st))
+        # prefill: shard 4 sequences by tokens
+        lens = [40, 70, 3, 90]
+        p = gi.prefill_inputs(lens, seed=4)
+        q0, q1, t0, t1, lcu = seq_shard(p["cu_seqlens"], world, rank)
+        po, ps = oracle.prefill(p["q"][t0:t1], p["k"][t0:t1], p["v"][t0:t1], p["state"][q0:q1], p["A_log"],
+                                p["a"][t0:t1], p["dt_bias"], p["b"][t0:t1], np.array(lcu), p["scale"], threads=1)
+        pre = [None] * world
+        dist.all_gather_object(pre, (po, ps))
+        t = torch.tensor([float(rank + 1)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            q.put((dec, pre, float(t.item())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_two_rank_sharded_oracle_matches_single_process():
+    from oracle import oracle
+    from tests.golden import inputs as gi
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    dec, pre, tmax = q.get()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert tmax == float(world)
+    d = gi.decode_inputs(6, seed=3)
+    fo, fs = oracle.decode(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"], d["scale"])
+    assert np.array_equal(np.concatenate([x[0] for x in dec]), fo)
+    assert np.array_equal(np.concatenate([x[1] for x in dec]), fs)
+    p = gi.prefill_inputs([40, 70, 3, 90], seed=4)
+    po, ps = oracle.prefill(p["q"], p["k"], p["v"], p["state"], p["A_log"], p["a"], p["dt_bias"], p["b"],
+                            p["cu_seqlens"], p["scale"])
+    assert np.array_equal(np.concatenate([x[0] for x in pre]), po)
+    assert np.array_equal(np.concatenate([x[1] for x in pre]), ps)
