@@ -1,0 +1,57 @@
+// noalloc.cu -- prefill entry point for callers that cannot allocate device memory.
+//
+// gdn_prefill_fwd needs a caller-provided workspace (w, u, Aqk, G: about 7.2 KB per token).
+// Some callers cannot provide one: a host runtime that owns every byte of device memory and
+// forbids plugins from calling cudaMalloc, a serving loop whose memory budget is fixed at
+// start-up, or code that must not allocate while other work is in flight.  For them this file
+// keeps the workspace in a fixed, file-scope device array sized for GDN_NOALLOC_MAX_TOKENS
+// tokens; it is allocated when the library is loaded and held by every GPU that loads the
+// library until the process exits.
+//
+// Host code may not pass the array's name to a kernel: on the host it is a stand-in symbol,
+// not a device address.  The device address is looked up once per device with
+// cudaGetSymbolAddress (with that device current) on the first call and cached.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+constexpr size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+// Same regions and order as gdn::prefill_workspace_layout (w bf16, u f32, Aqk bf16, G f32).
+constexpr size_t kNoAllocBytes =
+    align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 128 * 2) + align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 128 * 4) +
+    align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 64 * 2) + align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 4);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+// Device address of g_noalloc_scratch per device (nullptr until set up).  Two threads setting up
+// the same device concurrently store the same value.
+void* g_scratch_addr[kMaxDevices];
+
+}  // namespace
+
+extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v, const float* state,
+                                       const float* A_log, const void* a, const float* dt_bias, const void* b,
+                                       const void* cu_seqlens, int cu_is_int64, int N, int T, float scale, void* out,
+                                       float* new_state, int H, int HV, int K, int V, void* stream, unsigned flags) {
+    if (T < 0 || T > GDN_NOALLOC_MAX_TOKENS) return GDN_ERR_SIZE;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxDevices) return GDN_ERR_DEVICE;
+    if (g_scratch_addr[dev] == nullptr && T > 0) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return GDN_ERR_CUDA;
+        }
+        g_scratch_addr[dev] = p;
+    }
+    const size_t need = gdn_prefill_workspace_bytes(N, T, H, HV, K, V);
+    return gdn_prefill_fwd(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_is_int64, N, T, scale, out, new_state,
+                           T > 0 ? g_scratch_addr[dev] : nullptr, need, H, HV, K, V, stream, flags);
+}

@@ -108,6 +108,30 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
                     int N, int T, float scale, void* out, float* new_state, void* workspace, size_t workspace_bytes,
                     int H, int HV, int K, int V, void* stream, unsigned flags);
 
+/*
+ * Prefill without a workspace argument, for callers that cannot allocate device memory
+ * (a host runtime that owns all device memory and forbids its plugins from calling
+ * cudaMalloc, or a serving loop whose memory is fixed at start-up).  This entry point has
+ * no counterpart in the reference.
+ *
+ * Same arguments and results as gdn_prefill_fwd minus `workspace` / `workspace_bytes`: the
+ * workspace is a fixed device array inside the library, sized for GDN_NOALLOC_MAX_TOKENS
+ * packed tokens (about 14.7 MB), which every GPU that loads the library holds until the
+ * process exits.  T > GDN_NOALLOC_MAX_TOKENS returns GDN_ERR_SIZE and launches nothing.
+ * The call itself allocates nothing (no cudaMalloc / cudaFree).
+ * The first call on each device (with that device current) looks up the array's device
+ * address once; make that first call before any stream capture.
+ * All calls share the one array: calls that can overlap on the GPU (different streams,
+ * or different host threads) race on it and must be serialised by the caller.  No part of
+ * the array needs to start at zero: every location a call reads was written earlier in
+ * the same call.
+ */
+#define GDN_NOALLOC_MAX_TOKENS 2048
+int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                            const void* a, const float* dt_bias, const void* b, const void* cu_seqlens,
+                            int cu_is_int64, int N, int T, float scale, void* out, float* new_state, int H, int HV,
+                            int K, int V, void* stream, unsigned flags);
+
 /* Human-readable name of a status code (static storage). */
 const char* gdn_status_string(int status);
 
