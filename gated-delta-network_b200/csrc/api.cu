@@ -80,15 +80,13 @@ int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* sta
 
 size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV, int K, int V) {
     if (!shape_ok(H, HV, K, V) || N < 0 || T < 0) return 0;
-    size_t ow, ou, oa, og;
-    return gdn::prefill_workspace_layout(T, &ow, &ou, &oa, &og);
+    return gdn::prefill_layout(N, T).total;
 }
 
 int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state, const float* A_log,
                     const void* a, const float* dt_bias, const void* b, const void* cu_seqlens, int cu_is_int64,
                     int N, int T, float scale, void* out, float* new_state, void* workspace, size_t workspace_bytes,
                     int H, int HV, int K, int V, void* stream, unsigned flags) {
-    (void)flags;
     if (!shape_ok(H, HV, K, V)) return GDN_ERR_SHAPE;
     if (N < 0 || T < 0) return GDN_ERR_SIZE;
     if (N == 0) return GDN_OK;
@@ -98,9 +96,8 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
         (state && !aligned16(state)))
         return GDN_ERR_ALIGN;
     if (cu_is_int64 != 0 && cu_is_int64 != 1) return GDN_ERR_SIZE;
-    size_t ow, ou, oa, og;
-    const size_t need = gdn::prefill_workspace_layout(T, &ow, &ou, &oa, &og);
-    if (T > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
+    const gdn::PrefillLayout lay = gdn::prefill_layout(N, T);
+    if (!workspace || workspace_bytes < lay.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return GDN_ERR_WORKSPACE;
     int rc = check_device();
     if (rc != GDN_OK) return rc;
@@ -118,16 +115,20 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.cu64 = cu_is_int64;
     p.N = N;
     p.T = T;
+    p.S = lay.S;
     p.scale = scale;
     p.out = static_cast<uint16_t*>(out);
     p.new_state = new_state;
-    p.w = T > 0 ? reinterpret_cast<uint16_t*>(ws + ow) : nullptr;
-    p.u = T > 0 ? reinterpret_cast<float*>(ws + ou) : nullptr;
-    p.aqk = T > 0 ? reinterpret_cast<uint16_t*>(ws + oa) : nullptr;
-    p.g = T > 0 ? reinterpret_cast<float*>(ws + og) : nullptr;
+    p.status = reinterpret_cast<int*>(ws + lay.off_status);
+    p.chunk_base = reinterpret_cast<int*>(ws + lay.off_base);
+    p.chunk_seq = reinterpret_cast<int*>(ws + lay.off_seq);
+    p.w = reinterpret_cast<uint16_t*>(ws + lay.off_w);
+    p.u = reinterpret_cast<float*>(ws + lay.off_u);
+    p.aqk = reinterpret_cast<uint16_t*>(ws + lay.off_aqk);
+    p.g4 = reinterpret_cast<float*>(ws + lay.off_g4);
     const unsigned forced_bv = (flags >> 8) & 0xffu;
     const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N);
-    if (bv != 16 && bv != 32) return GDN_ERR_SIZE;
+    if (bv != 8 && bv != 16 && bv != 32) return GDN_ERR_SIZE;
     if (gdn::launch_prefill(p, bv, static_cast<cudaStream_t>(stream)) != 0) return GDN_ERR_CUDA;
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }

@@ -34,19 +34,57 @@ struct PrefillArgs {
     const void* cu;        // [N+1] int32 / int64
     int cu64;
     int N, T;
+    int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
     float scale;
     uint16_t* out;         // [T, 8, 128]
     float* new_state;      // [N, 8, 128, 128]
-    // workspace regions (head-major, token-indexed)
-    uint16_t* w;           // [8][T][128] bf16
-    float* u;              // [8][T][128] f32
-    uint16_t* aqk;         // [8][T][64] bf16
-    float* g;              // [8][T] f32 (chunk-local cumulative log decay)
+    // workspace (slot-indexed: slot s holds one 64-token chunk of one sequence; rows past the
+    // chunk end are zero / finite padding)
+    int* status;           // [1] first error code of a bounded wait that gave up (0 = none)
+    int* chunk_base;       // [N+1] first slot of each sequence (prefix sum of its chunk counts)
+    int* chunk_seq;        // [S]   sequence owning each slot, -1 for unused slots
+    uint16_t* w;           // [8][S*64][128] bf16   w = T diag(beta e^G) K
+    float* u;              // [8][S*64][128] f32    u = beta v + (T - I) diag(beta) V
+    uint16_t* aqk;         // [8][S*64][64]  bf16   masked, decayed Q K^T
+    float* g4;             // [8][S*64][4]   f32    {G, e^G, beta, 0}
+};
+
+// Byte offsets of the workspace regions for N sequences and T tokens.
+struct PrefillLayout {
+    int S;
+    size_t off_status, off_base, off_seq, off_w, off_u, off_aqk, off_g4, total;
 };
 
 int launch_decode(const DecodeArgs& p, int variant, cudaStream_t stream);
 int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream);
-size_t prefill_workspace_layout(int T, size_t* off_w, size_t* off_u, size_t* off_a, size_t* off_g);
+// Slots: one per 64-token chunk of each sequence.  sum_n ceil(len_n / 64) <= T/64 + N, and
+// every chunk holds at least one token, so min(T/64 + N, T) slots always suffice.
+__host__ __device__ constexpr size_t prefill_up256(size_t x) { return (x + 255) & ~(size_t)255; }
+__host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T) {
+    PrefillLayout L{};
+    long long S = (long long)T / 64 + N;
+    if (S > T) S = T;
+    if (S < 1) S = 1;
+    L.S = (int)S;
+    const size_t rows = (size_t)S * 64;
+    size_t o = 0;
+    L.off_status = o;
+    o = prefill_up256(o + 16);
+    L.off_base = o;
+    o = prefill_up256(o + sizeof(int) * ((size_t)N + 1));
+    L.off_seq = o;
+    o = prefill_up256(o + sizeof(int) * (size_t)S);
+    L.off_w = o;
+    o = prefill_up256(o + (size_t)8 * rows * 128 * 2);
+    L.off_u = o;
+    o = prefill_up256(o + (size_t)8 * rows * 128 * 4);
+    L.off_aqk = o;
+    o = prefill_up256(o + (size_t)8 * rows * 64 * 2);
+    L.off_g4 = o;
+    o = prefill_up256(o + (size_t)8 * rows * 4 * 4);
+    L.total = o;
+    return L;
+}
 int prefill_scan_bv(int N);
 
 }  // namespace gdn

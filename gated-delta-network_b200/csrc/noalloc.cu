@@ -5,7 +5,7 @@
 // forbids plugins from calling cudaMalloc, a serving loop whose memory budget is fixed at
 // start-up, or code that must not allocate while other work is in flight.  For them this file
 // keeps the workspace in a fixed, file-scope device array sized for GDN_NOALLOC_MAX_TOKENS
-// tokens; it is allocated when the library is loaded and held by every GPU that loads the
+// tokens in at most GDN_NOALLOC_MAX_SEQS sequences; it is allocated when the library is loaded and held by every GPU that loads the
 // library until the process exits.
 //
 // Host code may not pass the array's name to a kernel: on the host it is a stand-in symbol,
@@ -20,11 +20,8 @@
 
 namespace {
 
-constexpr size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
-// Same regions and order as gdn::prefill_workspace_layout (w bf16, u f32, Aqk bf16, G f32).
-constexpr size_t kNoAllocBytes =
-    align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 128 * 2) + align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 128 * 4) +
-    align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 64 * 2) + align256((size_t)8 * GDN_NOALLOC_MAX_TOKENS * 4);
+// Largest workspace any accepted call needs (the layout grows with both N and T).
+constexpr size_t kNoAllocBytes = gdn::prefill_layout(GDN_NOALLOC_MAX_SEQS, GDN_NOALLOC_MAX_TOKENS).total;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
@@ -39,11 +36,11 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
                                        const float* A_log, const void* a, const float* dt_bias, const void* b,
                                        const void* cu_seqlens, int cu_is_int64, int N, int T, float scale, void* out,
                                        float* new_state, int H, int HV, int K, int V, void* stream, unsigned flags) {
-    if (T < 0 || T > GDN_NOALLOC_MAX_TOKENS) return GDN_ERR_SIZE;
+    if (T < 0 || N < 0 || T > GDN_NOALLOC_MAX_TOKENS || N > GDN_NOALLOC_MAX_SEQS) return GDN_ERR_SIZE;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return GDN_ERR_DEVICE;
-    if (g_scratch_addr[dev] == nullptr && T > 0) {
+    if (g_scratch_addr[dev] == nullptr) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
             cudaGetLastError();
@@ -53,5 +50,5 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
     }
     const size_t need = gdn_prefill_workspace_bytes(N, T, H, HV, K, V);
     return gdn_prefill_fwd(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_is_int64, N, T, scale, out, new_state,
-                           T > 0 ? g_scratch_addr[dev] : nullptr, need, H, HV, K, V, stream, flags);
+                           g_scratch_addr[dev], need, H, HV, K, V, stream, flags);
 }

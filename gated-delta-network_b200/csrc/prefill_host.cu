@@ -1,0 +1,136 @@
+// prefill_host.cu -- workspace layout, chunk table kernel, TMA tensor maps and the launch
+// sequence of the chunked prefill (table -> prep -> scan), all on the caller's stream.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "prefill_kernels.cuh"
+
+namespace gdn {
+
+int prefill_scan_bv(int N) {
+    // (128 / BV) * N * 8 CTAs: small batches split the state columns finer to cover the SMs.
+    if (N * kHV * (kD / 32) >= 296) return 32;
+    if (N * kHV * (kD / 16) >= 148) return 16;
+    return 8;
+}
+
+// ---- chunk table ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) gdn_prefill_table_kernel(PrefillArgs p) {
+    __shared__ int s_warp[32];
+    __shared__ int s_total;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) *p.status = 0;
+    int running = 0;
+    for (int base = 0; base < p.N; base += 1024) {
+        const int i = base + tid;
+        int nc = 0;
+        if (i < p.N) {
+            int s, e;
+            seq_bounds(p.cu, p.cu64, i, p.T, s, e);
+            nc = (e - s + kChunk - 1) / kChunk;
+        }
+        int x = nc;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, off);
+            if (lane >= off) x += y;
+        }
+        if (lane == 31) s_warp[warp] = x;
+        __syncthreads();
+        int wpre = 0, total = 0;
+        for (int w = 0; w < 32; ++w) {
+            const int c = s_warp[w];
+            if (w < warp) wpre += c;
+            total += c;
+        }
+        if (i < p.N) p.chunk_base[i] = running + wpre + x - nc;
+        running += total;
+        __syncthreads();
+    }
+    if (tid == 0) {
+        p.chunk_base[p.N] = running;
+        s_total = running;
+    }
+    __syncthreads();
+    const int total = s_total;
+    for (int i = tid; i < p.N; i += 1024) {
+        int s, e;
+        seq_bounds(p.cu, p.cu64, i, p.T, s, e);
+        const int nc = (e - s + kChunk - 1) / kChunk;
+        const int b0 = p.chunk_base[i];
+        for (int c = 0; c < nc && b0 + c < p.S; ++c) p.chunk_seq[b0 + c] = i;
+    }
+    for (int s = total + tid; s < p.S; s += 1024) p.chunk_seq[s] = -1;
+}
+
+// ---- TMA tensor maps -----------------------------------------------------------------------
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn g_encode = nullptr;  // resolved once; concurrent resolution stores the same pointer
+
+EncodeTiledFn encode_fn() {
+    if (g_encode == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    return g_encode;
+}
+
+bool map3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t d0, uint64_t d1, uint64_t d2,
+           uint64_t stride1, uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1, stride2};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool build_prefill_maps(const PrefillArgs& p, int bv, PrefillMaps* m) {
+    const uint64_t T = (uint64_t)p.T, R = (uint64_t)p.S * kChunk;
+    const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+    const auto NS = CU_TENSOR_MAP_SWIZZLE_NONE;
+    // Inputs: [T][heads][128] bf16 as (col, head, token); one box = 64 columns x 1 head x 64 tokens.
+    bool ok = map3d(&m->q, p.q, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
+    ok = ok && map3d(&m->k, p.k, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
+    ok = ok && map3d(&m->v, p.v, BF, 128, kHV, T, 256, 256 * kHV, 64, 1, 64, SW);
+    // Workspace: [8][R][cols] as (col, row, head); one box = one 64-row chunk slot.
+    ok = ok && map3d(&m->w, p.w, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
+    ok = ok && map3d(&m->aqk, p.aqk, BF, 64, R, kHV, 128, R * 128, 64, 64, 1, SW);
+    ok = ok && map3d(&m->u, p.u, F32, 128, R, kHV, 512, R * 512, (uint32_t)bv, 64, 1, NS);
+    ok = ok && map3d(&m->g4, p.g4, F32, 4, R, kHV, 16, R * 16, 4, 64, 1, NS);
+    return ok;
+}
+
+int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream) {
+    if (p.N <= 0) return 0;
+    gdn_prefill_table_kernel<<<1, 1024, 0, stream>>>(p);
+    if (p.T > 0) {
+        PrefillMaps maps;
+        if (!build_prefill_maps(p, bv, &maps)) return -3;
+        if (launch_prefill_prep(p, maps, stream) != 0) return -1;
+        if (launch_prefill_scan(p, maps, bv, stream) != 0) return -1;
+    } else {
+        if (launch_prefill_scan(p, PrefillMaps{}, bv, stream) != 0) return -1;
+    }
+    return 0;
+}
+
+}  // namespace gdn

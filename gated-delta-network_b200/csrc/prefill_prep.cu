@@ -1,0 +1,375 @@
+// prefill_prep.cu -- chunk-parallel half of the chunked Gated DeltaNet prefill (sm_100a).
+//
+// One CTA per (64-token chunk slot, v-head), 128 threads, two CTAs per SM.  For the chunk's
+// tokens t = bos .. bos+L-1 of v-head hv (q/k head hv/2) it computes, following the chunked
+// WY form of solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/fla_kernels.py
+// (cumsum + K K^T 858-905, solve_tril 197-314, recompute_w_u 334-383):
+//   G_i   = sum_{t<=i} g_t              g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+//   A_ij  = beta_i e^{G_i-G_j} k_i.k_j  (i > j)          Aqk_ij = e^{G_i-G_j} q_i.k_j  (i >= j)
+//   T     = (I + A)^-1
+//   w     = T diag(beta e^G) K          u = beta v + (T - I) diag(beta) V
+// Data path:
+//   * TMA (SWIZZLE_128B boxes, no multicast) brings K, Q (qk head) and V (v-head) tiles.
+//   * tcgen05 MMA #1 (M=128, N=64, K=128): [K; Q] x K^T -> TMEM, rows 0-63 K K^T, 64-127 Q K^T.
+//   * Epilogue: one thread per TMEM lane turns its row into a row of A (fp32, shared memory)
+//     or of Aqk (bf16, global).
+//   * T = (I + A)^-1: 16x16 diagonal blocks by forward substitution (one column per lane),
+//     off-diagonal blocks T_ib,jb = -T_ib,ib sum_k A_ib,k T_k,jb with tf32 mma.sync.
+//   * tcgen05 MMA #2 (M=128, N=256, K=64): [T diag(beta e^G); (T - I) diag(beta)] x [K | V]
+//     -> TMEM; rows 0-63 / columns 0-127 are w, rows 64-127 / columns 128-255 are u - beta v.
+//   * Outputs go to the chunk's workspace slot; rows past the chunk end are written as zeros.
+#include "prefill_kernels.cuh"
+#include "sm100.cuh"
+
+namespace gdn {
+namespace prep2 {
+constexpr int kThreads = 128;
+constexpr int kFS = 68;  // fp32 row stride of A / T (rows stay 16-byte aligned)
+constexpr uint32_t kOffK0 = 0;        // K cols 0-63   (64 rows x 128 B, SW128)
+constexpr uint32_t kOffQ0 = 8192;     // Q cols 0-63   -> [K;Q] is one 128-row operand
+constexpr uint32_t kOffK1 = 16384;    // K cols 64-127
+constexpr uint32_t kOffQ1 = 24576;    // Q cols 64-127
+constexpr uint32_t kOffV0 = 32768;    // V cols 0-63   -> K0, K1, V0, V1 are 16 KB apart
+constexpr uint32_t kOffMisc = 40960;  // 8 KB: scratch, gates, barriers
+constexpr uint32_t kOffV1 = 49152;    // V cols 64-127
+constexpr uint32_t kOffA = 57344;     // A fp32 [64][68]; later [Wb; Ub] bf16 [128][64] SW128
+constexpr uint32_t kOffT = kOffA + 64 * kFS * 4;  // T fp32 [64][68]
+constexpr uint32_t kSmemUsed = kOffT + 64 * kFS * 4;
+constexpr uint32_t kSmem = kSmemUsed + 1024;  // slack for 1024-byte alignment
+// inside the misc block
+constexpr uint32_t kOffY = 0;                  // [4 warps][16][17] f32
+constexpr uint32_t kOffG = kOffY + 4 * 16 * 17 * 4;
+constexpr uint32_t kOffB = kOffG + 64 * 4;
+constexpr uint32_t kOffE = kOffB + 64 * 4;
+constexpr uint32_t kOffBar = kOffE + 64 * 4;   // 2 mbarriers
+constexpr uint32_t kOffSlot = kOffBar + 16;
+static_assert(kOffSlot + 16 <= 8192, "misc block");
+constexpr uint32_t kTmemCols = 256;
+}  // namespace prep2
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(prep2::kThreads, 2)
+    gdn_prefill_prep2_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
+    using namespace prep2;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(sm);
+    float* Af = reinterpret_cast<float*>(sm + kOffA);
+    float* Tf = reinterpret_cast<float*>(sm + kOffT);
+    unsigned char* misc = sm + kOffMisc;
+    float* Ysc = reinterpret_cast<float*>(misc + kOffY);
+    float* Gs = reinterpret_cast<float*>(misc + kOffG);
+    float* Bs = reinterpret_cast<float*>(misc + kOffB);
+    float* Es = reinterpret_cast<float*>(misc + kOffE);
+    uint64_t* bar_load = reinterpret_cast<uint64_t*>(misc + kOffBar);
+    uint64_t* bar_mma = bar_load + 1;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(misc + kOffSlot);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int gq = lane >> 2, tq = lane & 3;
+    const int slot = blockIdx.x, hv = blockIdx.y, hq = hv / (kHV / kH);
+    const int seq = p.chunk_seq[slot];
+    if (seq < 0) return;  // unused slot (uniform across the CTA)
+    int s0, e0;
+    seq_bounds(p.cu, p.cu64, seq, p.T, s0, e0);
+    const int bos = s0 + (slot - p.chunk_base[seq]) * kChunk;
+    const int L = min(kChunk, e0 - bos);
+    const size_t row0 = (size_t)hv * p.S * kChunk + (size_t)slot * kChunk;  // workspace row of token bos
+
+    // ---- 1. barriers, TMA loads, TMEM, gates ------------------------------------------------
+    if (tid == 0) {
+        mbar_init(bar_load, 1);
+        mbar_init(bar_mma, 1);
+        mbar_fence_init();
+    }
+    for (int i = tid; i < 64 * kFS; i += kThreads) Tf[i] = 0.f;
+    __syncthreads();
+    if (tid == 0) {
+        mbar_arrive_expect_tx(bar_load, 6 * 8192);
+        tma_load_3d(sm + kOffK0, &maps.k, 0, hq, bos, bar_load);
+        tma_load_3d(sm + kOffK1, &maps.k, 64, hq, bos, bar_load);
+        tma_load_3d(sm + kOffQ0, &maps.q, 0, hq, bos, bar_load);
+        tma_load_3d(sm + kOffQ1, &maps.q, 64, hq, bos, bar_load);
+        tma_load_3d(sm + kOffV0, &maps.v, 0, hv, bos, bar_load);
+        tma_load_3d(sm + kOffV1, &maps.v, 64, hv, bos, bar_load);
+    }
+    if (warp == 0) tmem_alloc(tslot, kTmemCols);
+    if (tid < 64) {
+        const int t = tid;
+        float gl = 0.f, be = 0.f;
+        if (t < L) {
+            const size_t tok = (size_t)(bos + t);
+            gl = log_decay(bf2f(p.a[tok * kHV + hv]), p.A_log[hv], p.dt_bias[hv]);
+            be = sigmoidf_(bf2f(p.b[tok * kHV + hv]));
+        }
+        float x = gl;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, x, off);
+            if (lane >= off) x += y;
+        }
+        Gs[t] = x;
+        Bs[t] = be;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    if (tid < 64) {
+        // padded tokens (t >= L) carry g = 0, so their cumulative G repeats G_{L-1}
+        float x = Gs[tid];
+        if (tid >= 32) x += Gs[31];
+        Es[tid] = __expf(x);
+        Gs[tid] = x;  // warp 0 rewrites Gs[0..31] unchanged; warp 1 only reads Gs[31]
+    }
+    bool ok = mbar_wait(bar_load, 0, p.status, kErrPrepTmaTimeout);
+    ok = __syncthreads_and(ok);  // also publishes Gs / Es
+    if (!ok) goto cleanup;
+
+    // ---- 2. MMA #1: [K; Q] (128 x 128) x K^T -> TMEM columns 0..63 ---------------------------
+    if (tid == 0) {
+        tc_fence_after();
+        constexpr uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t koff = (uint32_t)(kk >> 2) * (kOffK1 - kOffK0) + (uint32_t)(kk & 3) * 32u;
+            umma_bf16(tmem, umma_desc_sw128(sbase + kOffK0 + koff, 16, 1024),
+                      umma_desc_sw128(sbase + kOffK0 + koff, 16, 1024), idesc, kk > 0);
+        }
+        umma_commit(bar_mma);
+    }
+    ok = mbar_wait(bar_mma, 0, p.status, kErrPrepMmaTimeout);
+    ok = __syncthreads_and(ok);
+    if (!ok) goto cleanup;
+    tc_fence_after();
+
+    // ---- 3. epilogue #1: thread r owns TMEM lane r (rows 0-63: K K^T, rows 64-127: Q K^T) -----
+    {
+        const int r = tid, i = r & 63;
+        const bool qk = r >= 64;
+        const float Gi = Gs[i], bi = Bs[i];
+        const bool live = i < L;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            float d[32];
+            tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 32 * half, d);
+            if (!qk) {
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    float4 o;
+                    float* po = &o.x;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = 32 * half + 4 * j4 + e;
+                        po[e] = (live && j < i) ? bi * __expf(Gi - Gs[j]) * d[4 * j4 + e] : 0.f;
+                    }
+                    *reinterpret_cast<float4*>(Af + i * kFS + 32 * half + 4 * j4) = o;
+                }
+            } else {
+                uint16_t* dst = p.aqk + (row0 + i) * 64 + 32 * half;
+#pragma unroll
+                for (int j8 = 0; j8 < 4; ++j8) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j0 = 32 * half + 8 * j8 + 2 * e;
+                        const float x0 = (live && j0 <= i) ? __expf(Gi - Gs[j0]) * d[8 * j8 + 2 * e] : 0.f;
+                        const float x1 = (live && j0 + 1 <= i) ? __expf(Gi - Gs[j0 + 1]) * d[8 * j8 + 2 * e + 1] : 0.f;
+                        pk[e] = pack_bf16x2(x0, x1);
+                    }
+                    *reinterpret_cast<uint4*>(dst + 8 * j8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+            }
+        }
+        if (tid < 64) *reinterpret_cast<float4*>(p.g4 + (row0 + tid) * 4) = make_float4(Gs[tid], Es[tid], Bs[tid], 0.f);
+    }
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- 4. T = (I + A)^-1 ----------------------------------------------------------------
+    // 4a. diagonal 16x16 blocks: warp w inverts block w, lanes 0..15 each own one column.
+    {
+        const int jb = warp;
+        const float* Ab = Af + (16 * jb) * kFS + 16 * jb;
+        if (lane < 16) {
+            float x[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r) x[r] = (r == lane) ? 1.f : 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float xi = x[i];
+#pragma unroll
+                for (int m = i + 1; m < 16; ++m) x[m] = fmaf(-Ab[m * kFS + i], xi, x[m]);
+            }
+            float* Tb = Tf + (16 * jb) * kFS + 16 * jb;
+#pragma unroll
+            for (int r = 0; r < 16; ++r) Tb[r * kFS + lane] = x[r];
+        }
+    }
+    __syncthreads();
+    // 4b. off-diagonal blocks of column block jb = warp:
+    //     T_ib,jb = -T_ib,ib * sum_{kb=jb}^{ib-1} A_ib,kb T_kb,jb   (tf32 MMAs, fp32 accumulate)
+    {
+        const int jb = warp;
+        float* Y = Ysc + warp * 16 * 17;
+        for (int ib = jb + 1; ib < 4; ++ib) {
+            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            for (int kb = jb; kb < ib; ++kb) {
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks) {
+                    const float* As_ = Af + (16 * ib) * kFS + 16 * kb + 8 * ks;
+                    const uint32_t a[4] = {to_tf32(As_[gq * kFS + tq]), to_tf32(As_[(gq + 8) * kFS + tq]),
+                                           to_tf32(As_[gq * kFS + tq + 4]), to_tf32(As_[(gq + 8) * kFS + tq + 4])};
+                    const float* Bm = Tf + (16 * kb + 8 * ks) * kFS + 16 * jb;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+                        mma_tf32(acc[nt], a, to_tf32(Bm[tq * kFS + 8 * nt + gq]),
+                                 to_tf32(Bm[(tq + 4) * kFS + 8 * nt + gq]));
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                Y[gq * 17 + 8 * nt + 2 * tq] = acc[nt][0];
+                Y[gq * 17 + 8 * nt + 2 * tq + 1] = acc[nt][1];
+                Y[(gq + 8) * 17 + 8 * nt + 2 * tq] = acc[nt][2];
+                Y[(gq + 8) * 17 + 8 * nt + 2 * tq + 1] = acc[nt][3];
+            }
+            __syncwarp();
+            float rr[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            const float* Dm = Tf + (16 * ib) * kFS + 16 * ib;
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks) {
+                const uint32_t a[4] = {to_tf32(Dm[gq * kFS + 8 * ks + tq]), to_tf32(Dm[(gq + 8) * kFS + 8 * ks + tq]),
+                                       to_tf32(Dm[gq * kFS + 8 * ks + tq + 4]),
+                                       to_tf32(Dm[(gq + 8) * kFS + 8 * ks + tq + 4])};
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+                    mma_tf32(rr[nt], a, to_tf32(Y[(8 * ks + tq) * 17 + 8 * nt + gq]),
+                             to_tf32(Y[(8 * ks + tq + 4) * 17 + 8 * nt + gq]));
+            }
+            float* Tout = Tf + (16 * ib) * kFS + 16 * jb;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                Tout[gq * kFS + 8 * nt + 2 * tq] = -rr[nt][0];
+                Tout[gq * kFS + 8 * nt + 2 * tq + 1] = -rr[nt][1];
+                Tout[(gq + 8) * kFS + 8 * nt + 2 * tq] = -rr[nt][2];
+                Tout[(gq + 8) * kFS + 8 * nt + 2 * tq + 1] = -rr[nt][3];
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+
+    // ---- 5. MMA #2 operand [T diag(beta e^G); (T - I) diag(beta)]: bf16 [128][64] SW128 -----
+    {
+        const int r = tid, m = r & 63;
+        const bool ub = r >= 64;
+        const float* Trow = Tf + m * kFS;
+        unsigned char* dst = sm + kOffA + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 8 * c + 2 * e;
+                float t0 = Trow[j], t1 = Trow[j + 1];
+                if (ub) {
+                    t0 = (j == m ? t0 - 1.f : t0) * Bs[j];
+                    t1 = (j + 1 == m ? t1 - 1.f : t1) * Bs[j + 1];
+                } else {
+                    t0 *= Bs[j] * Es[j];
+                    t1 *= Bs[j + 1] * Es[j + 1];
+                }
+                pk[e] = pack_bf16x2(t0, t1);
+            }
+            *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- 6. MMA #2: [Wb; Ub] (128 x 64) x [K | V] (64 x 256, N-major) -> TMEM columns 0..255 --
+    if (tid == 0) {
+        tc_fence_after();
+        constexpr uint32_t idesc = umma_idesc_bf16(128, 256, false, true);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem, umma_desc_sw128(sbase + kOffA + 32u * kk, 16, 1024),
+                      umma_desc_sw128(sbase + kOffK0 + 2048u * kk, kOffK1 - kOffK0, 1024), idesc, kk > 0);
+        umma_commit(bar_mma);
+    }
+    ok = mbar_wait(bar_mma, 1, p.status, kErrPrepMmaTimeout);
+    ok = __syncthreads_and(ok);
+    if (!ok) goto cleanup;
+    tc_fence_after();
+
+    // ---- 7. epilogue #2: rows 0-63 -> w (bf16), rows 64-127 -> u = D + beta v (f32) ---------
+    {
+        const int r = tid;
+        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+        if (r < 64) {
+            uint16_t* dst = p.w + (row0 + r) * kD;
+#pragma unroll 1
+            for (int cb = 0; cb < 4; ++cb) {
+                float d[32];
+                tmem_ld32(tl + 32 * cb, d);
+#pragma unroll
+                for (int j8 = 0; j8 < 4; ++j8)
+                    *reinterpret_cast<uint4*>(dst + 32 * cb + 8 * j8) =
+                        make_uint4(pack_bf16x2(d[8 * j8], d[8 * j8 + 1]), pack_bf16x2(d[8 * j8 + 2], d[8 * j8 + 3]),
+                                   pack_bf16x2(d[8 * j8 + 4], d[8 * j8 + 5]), pack_bf16x2(d[8 * j8 + 6], d[8 * j8 + 7]));
+            }
+        } else {
+            const int m = r - 64;
+            const float be = Bs[m];
+            float* dst = p.u + (row0 + m) * kD;
+            const unsigned char* vt = sm + kOffV0;
+#pragma unroll 1
+            for (int cb = 0; cb < 4; ++cb) {
+                float d[32];
+                tmem_ld32(tl + 128 + 32 * cb, d);
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const int c = 32 * cb + 4 * j4;
+                    const uint2 vv = *reinterpret_cast<const uint2*>(vt + sw128_off(m, c, kOffV1 - kOffV0));
+                    float4 o;
+                    o.x = fmaf(be, __uint_as_float(vv.x << 16), d[4 * j4 + 0]);
+                    o.y = fmaf(be, __uint_as_float(vv.x & 0xffff0000u), d[4 * j4 + 1]);
+                    o.z = fmaf(be, __uint_as_float(vv.y << 16), d[4 * j4 + 2]);
+                    o.w = fmaf(be, __uint_as_float(vv.y & 0xffff0000u), d[4 * j4 + 3]);
+                    *reinterpret_cast<float4*>(dst + c) = o;
+                }
+            }
+        }
+    }
+
+cleanup:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream) {
+    using namespace prep2;
+    if (cudaFuncSetAttribute(gdn_prefill_prep2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
+        cudaSuccess)
+        return -1;
+    dim3 grid((unsigned)p.S, kHV);
+    gdn_prefill_prep2_kernel<<<grid, kThreads, kSmem, stream>>>(p, maps);
+    return 0;
+}
+
+}  // namespace gdn

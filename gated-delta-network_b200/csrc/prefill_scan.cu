@@ -1,0 +1,321 @@
+// prefill_scan.cu -- serial half of the chunked Gated DeltaNet prefill (sm_100a).
+//
+// One CTA per (slice of BV state columns, sequence n, v-head hv); it walks the chunks of
+// sequence n in order and keeps its [K=128 x BV] slice of the state h in registers (fp32
+// mma.sync accumulator fragments) for the whole sequence.  Per chunk (fused form of
+// solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/fla_kernels.py:411-671 chunk_h
+// and 714-796 chunk_o; the per-chunk state snapshots never leave the SM):
+//   vn = u - w h                                  (u, w from the prep kernel's workspace slot)
+//   o  = scale (e^G . (Q h) + Aqk vn)             -> out
+//   h  = e^{G_last} h + K^T (e^{G_last - G} . vn) (vn split into bf16 hi + lo: ~16-bit mantissa)
+// Each chunk's W, Q, K, Aqk (SWIZZLE_128B), u slice and G tiles arrive by TMA (one thread
+// issues them) into a 3-stage ring of shared-memory buffers tracked by mbarriers, two chunks
+// ahead of the math.  The serial dependency (w h -> vn -> K^T vn -> h) uses warp-level
+// mma.sync fragments: their ~20-cycle latency beats a tcgen05 round trip (~570 cycles) for
+// these 64 x BV x 128 products, and the state never has to leave the register file.
+#include "prefill_kernels.cuh"
+#include "sm100.cuh"
+
+namespace gdn {
+
+template <int BV>
+struct Scan2Cfg {
+    static constexpr int kThreads = 128;
+    static constexpr int kStages = 3;
+    static constexpr int kHS = BV + 8;  // bf16 row stride of the [rows][BV] operand tiles
+    static constexpr uint32_t kOffW = 0;        // 2 atoms of 64 rows x 128 B (atom stride 8 KB)
+    static constexpr uint32_t kOffQ = 16384;
+    static constexpr uint32_t kOffK = 32768;
+    static constexpr uint32_t kOffA = 49152;    // Aqk: 1 atom
+    static constexpr uint32_t kOffU = 57344;    // [64][BV] f32
+    static constexpr uint32_t kOffG = kOffU + 64 * BV * 4;  // [64][4] f32 {G, e^G, beta, 0}
+    static constexpr uint32_t kStage = ((kOffG + 1024) + 1023) & ~1023u;
+    static constexpr uint32_t kTxBytes = 3 * 16384 + 8192 + 64 * BV * 4 + 1024;
+    static constexpr uint32_t kOffHb = kStages * kStage;               // [128][kHS] bf16
+    static constexpr uint32_t kOffVn = kOffHb + 128 * kHS * 2;          // [64][kHS] bf16
+    static constexpr uint32_t kOffVh = kOffVn + 64 * kHS * 2;
+    static constexpr uint32_t kOffVl = kOffVh + 64 * kHS * 2;
+    static constexpr uint32_t kOffBar = (kOffVl + 64 * kHS * 2 + 15) & ~15u;
+    static constexpr uint32_t kSmemUsed = kOffBar + 8 * kStages;
+    static constexpr uint32_t kSmem = kSmemUsed + 1024;
+    static_assert(kSmem <= 227 * 1024, "scan shared memory");
+};
+
+__device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
+}
+
+// B fragments (k16 x n8 tiles nt = 0..NT8-1) of a [k][kHS] bf16 row-major tile, rows k0..k0+15.
+template <int NT8, int HS>
+__device__ __forceinline__ void load_b_frags(uint32_t (&b)[NT8][2], const uint16_t* tile, int k0, int lane) {
+    if constexpr (NT8 == 1) {
+        ldsm_x2_t(b[0][0], b[0][1], tile + (k0 + (lane & 15)) * HS);
+    } else {
+#pragma unroll
+        for (int np = 0; np < NT8 / 2; ++np)
+            ldsm_x4_t(b[2 * np][0], b[2 * np][1], b[2 * np + 1][0], b[2 * np + 1][1],
+                      tile + (k0 + (lane & 7) + (((lane >> 3) & 1) << 3)) * HS + 16 * np + ((lane >> 4) << 3));
+    }
+}
+
+template <int BV>
+__global__ void __launch_bounds__(128, 1)
+    gdn_prefill_scan2_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
+    using C = Scan2Cfg<BV>;
+    constexpr int NT8 = BV / 8;
+    constexpr int HS = C::kHS;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint16_t* Hb = reinterpret_cast<uint16_t*>(sm + C::kOffHb);
+    uint16_t* VNb = reinterpret_cast<uint16_t*>(sm + C::kOffVn);
+    uint16_t* VNh = reinterpret_cast<uint16_t*>(sm + C::kOffVh);
+    uint16_t* VNl = reinterpret_cast<uint16_t*>(sm + C::kOffVl);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int gq = lane >> 2, tq = lane & 3;
+    const int v0 = blockIdx.x * BV;
+    const int n = blockIdx.y / kHV, hv = blockIdx.y % kHV, hq = hv / (kHV / kH);
+    int bos, eos;
+    seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
+    const int len = eos - bos;
+    float* st_out = p.new_state + ((size_t)n * kHV + hv) * kD * kD;
+
+    if (blockIdx.x == 0 && blockIdx.y == 0 && p.T > 0) {
+        // Tokens outside [cu[0], cu[N]) belong to no sequence: zero output, as the reference
+        // zero-initialises the whole output (reference/gdn_prefill_ref.py:49-51).
+        int lo, tmp, hi;
+        seq_bounds(p.cu, p.cu64, 0, p.T, lo, tmp);
+        seq_bounds(p.cu, p.cu64, p.N - 1, p.T, tmp, hi);
+        hi = max(hi, lo);
+        const size_t row_words = kHV * kD / 8;
+        uint4* o4 = reinterpret_cast<uint4*>(p.out);
+        for (size_t idx = tid; idx < (size_t)lo * row_words; idx += C::kThreads) o4[idx] = make_uint4(0, 0, 0, 0);
+        for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += C::kThreads)
+            o4[idx] = make_uint4(0, 0, 0, 0);
+    }
+    if (len <= 0) {  // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62)
+        for (int idx = tid; idx < BV * kD; idx += C::kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
+        return;
+    }
+    const int nchunks = (len + kChunk - 1) / kChunk;
+    const int slot0 = p.chunk_base[n];
+
+    auto issue = [&](int c) {
+        unsigned char* st = sm + (c % C::kStages) * C::kStage;
+        uint64_t* bar = full + (c % C::kStages);
+        const int slot = slot0 + c, t0 = bos + c * kChunk, wr = slot * kChunk;
+        mbar_arrive_expect_tx(bar, C::kTxBytes);
+        tma_load_3d(st + C::kOffW, &maps.w, 0, wr, hv, bar);
+        tma_load_3d(st + C::kOffW + 8192, &maps.w, 64, wr, hv, bar);
+        tma_load_3d(st + C::kOffQ, &maps.q, 0, hq, t0, bar);
+        tma_load_3d(st + C::kOffQ + 8192, &maps.q, 64, hq, t0, bar);
+        tma_load_3d(st + C::kOffK, &maps.k, 0, hq, t0, bar);
+        tma_load_3d(st + C::kOffK + 8192, &maps.k, 64, hq, t0, bar);
+        tma_load_3d(st + C::kOffA, &maps.aqk, 0, wr, hv, bar);
+        tma_load_3d(st + C::kOffU, &maps.u, v0, wr, hv, bar);
+        tma_load_3d(st + C::kOffG, &maps.g4, 0, wr, hv, bar);
+    };
+    if (tid == 0) {
+        for (int s = 0; s < C::kStages; ++s) mbar_init(full + s, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int c = 0; c < min(nchunks, C::kStages - 1); ++c) issue(c);
+    }
+
+    // state slice h[kdim][v] as mma C fragments: rows 32*warp + 16*mt + gq (+8), cols 8*nt + 2*tq (+1)
+    float h[2][NT8][4];
+    {
+        const float* st_in = p.state ? p.state + ((size_t)n * kHV + hv) * kD * kD : nullptr;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int row = 32 * warp + 16 * mt + gq + 8 * (e >> 1);
+                    const int col = 8 * nt + 2 * tq + (e & 1);
+                    h[mt][nt][e] = st_in ? st_in[(size_t)(v0 + col) * kD + row] : 0.f;
+                }
+    }
+    auto write_hb = [&]() {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int row = 32 * warp + 16 * mt + gq + 8 * half;
+                    *reinterpret_cast<uint32_t*>(Hb + row * HS + 8 * nt + 2 * tq) =
+                        pack_bf16x2(h[mt][nt][2 * half], h[mt][nt][2 * half + 1]);
+                }
+    };
+    write_hb();
+
+    int c = 0;
+    for (; c < nchunks; ++c) {
+        // The buffers of stage (c+2) % 3 were last read in chunk c-1, which every thread has
+        // finished (barrier at the end of the previous iteration): refill them with chunk c+2.
+        if (tid == 0 && c + C::kStages - 1 < nchunks) issue(c + C::kStages - 1);
+        bool ok = mbar_wait(full + (c % C::kStages), (uint32_t)((c / C::kStages) & 1), p.status, kErrScanTmaTimeout);
+        ok = __syncthreads_and(ok);  // also orders the previous iteration's Hb writes
+        if (!ok) break;
+
+        const unsigned char* st = sm + (c % C::kStages) * C::kStage;
+        const unsigned char* Ws = st + C::kOffW;
+        const unsigned char* Qs = st + C::kOffQ;
+        const unsigned char* Ks = st + C::kOffK;
+        const unsigned char* As = st + C::kOffA;
+        const float* Us = reinterpret_cast<const float*>(st + C::kOffU);
+        const float* G4 = reinterpret_cast<const float*>(st + C::kOffG);
+        const int t0 = bos + c * kChunk;
+        const int L = min(kChunk, eos - t0);
+        const float GL = G4[(L - 1) * 4];
+
+        // (1) P1 = W h, P2 = Q h   (rows 16*warp .. +15)
+        float p1[NT8][4], p2[NT8][4];
+#pragma unroll
+        for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) p1[nt][e] = p2[nt][e] = 0.f;
+#pragma unroll
+        for (int k0 = 0; k0 < 128; k0 += 16) {
+            uint32_t aw[4], aq[4], b[NT8][2];
+            const int ar = 16 * warp + (lane & 15), ac = k0 + ((lane >> 4) << 3);
+            ldsm_x4(aw[0], aw[1], aw[2], aw[3], Ws + sw128_off(ar, ac, 8192));
+            ldsm_x4(aq[0], aq[1], aq[2], aq[3], Qs + sw128_off(ar, ac, 8192));
+            load_b_frags<NT8, HS>(b, Hb, k0, lane);
+#pragma unroll
+            for (int nt = 0; nt < NT8; ++nt) {
+                mma_bf16(p1[nt], aw, b[nt][0], b[nt][1]);
+                mma_bf16(p2[nt], aq, b[nt][0], b[nt][1]);
+            }
+        }
+        // (2) vn = u - P1; o = scale e^G P2; stage vn (bf16) and the decayed vn (hi + lo)
+        float o[NT8][4];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int row = 16 * warp + gq + 8 * half;
+            const float eg = G4[row * 4 + 1];
+            const float ed = __expf(GL - G4[row * 4]);  // <= 1; padded rows have vn = 0
+#pragma unroll
+            for (int nt = 0; nt < NT8; ++nt) {
+                const int col = 8 * nt + 2 * tq;
+                const float2 uu = *reinterpret_cast<const float2*>(Us + row * BV + col);
+                const float vn0 = uu.x - p1[nt][2 * half];
+                const float vn1 = uu.y - p1[nt][2 * half + 1];
+                o[nt][2 * half] = p.scale * eg * p2[nt][2 * half];
+                o[nt][2 * half + 1] = p.scale * eg * p2[nt][2 * half + 1];
+                *reinterpret_cast<uint32_t*>(VNb + row * HS + col) = pack_bf16x2(vn0, vn1);
+                const float d0 = vn0 * ed, d1 = vn1 * ed;
+                const uint32_t hi = pack_bf16x2(d0, d1);
+                *reinterpret_cast<uint32_t*>(VNh + row * HS + col) = hi;
+                *reinterpret_cast<uint32_t*>(VNl + row * HS + col) =
+                    pack_bf16x2(d0 - __uint_as_float(hi << 16), d1 - __uint_as_float(hi & 0xffff0000u));
+            }
+        }
+        __syncthreads();
+
+        // (3a) o += scale Aqk vn; store the chunk's outputs
+        {
+            float acc[NT8][4];
+#pragma unroll
+            for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+#pragma unroll
+            for (int k0 = 0; k0 < 64; k0 += 16) {
+                uint32_t a[4], b[NT8][2];
+                ldsm_x4(a[0], a[1], a[2], a[3], As + sw128_off(16 * warp + (lane & 15), k0 + ((lane >> 4) << 3), 0));
+                load_b_frags<NT8, HS>(b, VNb, k0, lane);
+#pragma unroll
+                for (int nt = 0; nt < NT8; ++nt) mma_bf16(acc[nt], a, b[nt][0], b[nt][1]);
+            }
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int row = 16 * warp + gq + 8 * half;
+                if (row < L) {
+                    uint16_t* dst = p.out + ((size_t)(t0 + row) * kHV + hv) * kD + v0;
+#pragma unroll
+                    for (int nt = 0; nt < NT8; ++nt)
+                        *reinterpret_cast<uint32_t*>(dst + 8 * nt + 2 * tq) =
+                            pack_bf16x2(fmaf(p.scale, acc[nt][2 * half], o[nt][2 * half]),
+                                        fmaf(p.scale, acc[nt][2 * half + 1], o[nt][2 * half + 1]));
+                }
+            }
+        }
+        // (3b) h = e^{GL} h + K^T (vn_hi + vn_lo)   (rows 32*warp .. +31 of the K dimension)
+        {
+            const float eL = __expf(GL);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) h[mt][nt][e] *= eL;
+#pragma unroll
+            for (int k0 = 0; k0 < 64; k0 += 16) {
+                uint32_t a[2][4], bh[NT8][2], bl[NT8][2];
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+                    ldsm_x4_t(a[mt][0], a[mt][1], a[mt][2], a[mt][3],
+                              Ks + sw128_off(k0 + (lane & 7) + ((lane >> 4) << 3),
+                                             32 * warp + 16 * mt + (((lane >> 3) & 1) << 3), 8192));
+                load_b_frags<NT8, HS>(bh, VNh, k0, lane);
+                load_b_frags<NT8, HS>(bl, VNl, k0, lane);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < NT8; ++nt) {
+                        mma_bf16(h[mt][nt], a[mt], bh[nt][0], bh[nt][1]);
+                        mma_bf16(h[mt][nt], a[mt], bl[nt][0], bl[nt][1]);
+                    }
+            }
+        }
+        write_hb();
+        __syncthreads();
+    }
+    if (c < nchunks) {
+        // A TMA wait gave up: let the copies already issued land (bounded) before the CTA exits.
+        if (tid == 0)
+            for (int cc = c + 1; cc < min(nchunks, c + C::kStages); ++cc)
+                mbar_wait(full + (cc % C::kStages), (uint32_t)((cc / C::kStages) & 1), nullptr, 0);
+        return;
+    }
+
+    // final state (k-last): new_state[n][hv][v0 + col][row]
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = 32 * warp + 16 * mt + gq + 8 * (e >> 1);
+                const int col = 8 * nt + 2 * tq + (e & 1);
+                st_out[(size_t)(v0 + col) * kD + row] = h[mt][nt][e];
+            }
+}
+
+template <int BV>
+static int launch_scan_bv(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream) {
+    using C = Scan2Cfg<BV>;
+    if (cudaFuncSetAttribute(gdn_prefill_scan2_kernel<BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+        cudaSuccess)
+        return -1;
+    dim3 grid(kD / BV, p.N * kHV);
+    gdn_prefill_scan2_kernel<BV><<<grid, C::kThreads, C::kSmem, stream>>>(p, maps);
+    return 0;
+}
+
+int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream) {
+    switch (bv) {
+        case 8: return launch_scan_bv<8>(p, maps, stream);
+        case 16: return launch_scan_bv<16>(p, maps, stream);
+        case 32: return launch_scan_bv<32>(p, maps, stream);
+        default: return -2;
+    }
+}
+
+}  // namespace gdn

@@ -98,8 +98,10 @@ size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV, int K, int V);
  *   out         [T, HV, V]           bf16   (written for every token covered by a sequence)
  *   new_state   [N, HV, V, K]        f32    final state; a zero-length sequence gets all zeros
  *                                    (reference/gdn_prefill_ref.py:52-54, 61-62); may alias `state`
- *   workspace   >= gdn_prefill_workspace_bytes(N, T, ...) bytes of device memory, 256-byte aligned;
- *               no contents are carried between calls.
+ *   workspace   >= gdn_prefill_workspace_bytes(N, T, ...) bytes of device memory, 256-byte aligned,
+ *               required even when T == 0; no contents are carried between calls.  Its first
+ *               int receives 0, or the code of a bounded device-side wait that gave up
+ *               (the call's outputs are then invalid); reading it is optional.
  * Sequence bounds are clamped to [0, T] on the device, so malformed cu_seqlens
  * cannot make the kernels read or write outside the buffers.
  */
@@ -116,8 +118,9 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
  *
  * Same arguments and results as gdn_prefill_fwd minus `workspace` / `workspace_bytes`: the
  * workspace is a fixed device array inside the library, sized for GDN_NOALLOC_MAX_TOKENS
- * packed tokens (about 14.7 MB), which every GPU that loads the library holds until the
- * process exits.  T > GDN_NOALLOC_MAX_TOKENS returns GDN_ERR_SIZE and launches nothing.
+ * packed tokens in at most GDN_NOALLOC_MAX_SEQS sequences (about 22 MB), which every GPU
+ * that loads the library holds until the process exits.  T > GDN_NOALLOC_MAX_TOKENS or
+ * N > GDN_NOALLOC_MAX_SEQS returns GDN_ERR_SIZE and launches nothing.
  * The call itself allocates nothing (no cudaMalloc / cudaFree).
  * The first call on each device (with that device current) looks up the array's device
  * address once; make that first call before any stream capture.
@@ -127,6 +130,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
  * the same call.
  */
 #define GDN_NOALLOC_MAX_TOKENS 2048
+#define GDN_NOALLOC_MAX_SEQS 16
 int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v, const float* state, const float* A_log,
                             const void* a, const float* dt_bias, const void* b, const void* cu_seqlens,
                             int cu_is_int64, int N, int T, float scale, void* out, float* new_state, int H, int HV,

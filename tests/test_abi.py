@@ -39,7 +39,7 @@ def test_version_and_status_strings(lib):
 
 def test_workspace_bytes(lib):
     ws = lambda n, t: lib.gdn_prefill_workspace_bytes(n, t, 4, 8, 128, 128)
-    assert ws(1, 0) == 0
+    assert 0 < ws(1, 0) <= 1 << 20  # chunk table and status word only
     w1 = ws(1, 1024)
     # w (bf16) + u (f32) + Aqk (bf16, 64 wide) + G (f32), per token and v-head
     assert w1 >= 1024 * 8 * (128 * 2 + 128 * 4 + 64 * 2 + 4)
