@@ -124,7 +124,8 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.chunk_seq = reinterpret_cast<int*>(ws + lay.off_seq);
     p.w = reinterpret_cast<uint16_t*>(ws + lay.off_w);
     p.u = reinterpret_cast<float*>(ws + lay.off_u);
-    p.aqk = reinterpret_cast<uint16_t*>(ws + lay.off_aqk);
+    p.qp = reinterpret_cast<uint16_t*>(ws + lay.off_qp);
+    p.oi = reinterpret_cast<uint16_t*>(ws + lay.off_oi);
     p.g4 = reinterpret_cast<float*>(ws + lay.off_g4);
     const unsigned forced_bv = (flags >> 8) & 0xffu;
     const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N);

@@ -45,14 +45,15 @@ struct PrefillArgs {
     int* chunk_seq;        // [S]   sequence owning each slot, -1 for unused slots
     uint16_t* w;           // [8][S*64][128] bf16   w = T diag(beta e^G) K
     float* u;              // [8][S*64][128] f32    u = beta v + (T - I) diag(beta) V
-    uint16_t* aqk;         // [8][S*64][64]  bf16   masked, decayed Q K^T
+    uint16_t* qp;          // [8][S*64][128] bf16   Q' = diag(e^G) Q - Aqk w  (output operand)
+    uint16_t* oi;          // [8][S*64][128] bf16   oi = Aqk u                 (intra-chunk output)
     float* g4;             // [8][S*64][4]   f32    {G, e^G, beta, 0}
 };
 
 // Byte offsets of the workspace regions for N sequences and T tokens.
 struct PrefillLayout {
     int S;
-    size_t off_status, off_base, off_seq, off_w, off_u, off_aqk, off_g4, total;
+    size_t off_status, off_base, off_seq, off_w, off_u, off_qp, off_oi, off_g4, total;
 };
 
 int launch_decode(const DecodeArgs& p, int variant, cudaStream_t stream);
@@ -78,8 +79,10 @@ __host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T) {
     o = prefill_up256(o + (size_t)8 * rows * 128 * 2);
     L.off_u = o;
     o = prefill_up256(o + (size_t)8 * rows * 128 * 4);
-    L.off_aqk = o;
-    o = prefill_up256(o + (size_t)8 * rows * 64 * 2);
+    L.off_qp = o;
+    o = prefill_up256(o + (size_t)8 * rows * 128 * 2);
+    L.off_oi = o;
+    o = prefill_up256(o + (size_t)8 * rows * 128 * 2);
     L.off_g4 = o;
     o = prefill_up256(o + (size_t)8 * rows * 4 * 4);
     L.total = o;

@@ -5,8 +5,8 @@
 // forbids plugins from calling cudaMalloc, a serving loop whose memory budget is fixed at
 // start-up, or code that must not allocate while other work is in flight.  For them this file
 // keeps the workspace in a fixed, file-scope device array sized for GDN_NOALLOC_MAX_TOKENS
-// tokens in at most GDN_NOALLOC_MAX_SEQS sequences; it is allocated when the library is loaded and held by every GPU that loads the
-// library until the process exits.
+// tokens in at most GDN_NOALLOC_MAX_SEQS sequences; it is allocated when the library is
+// loaded and held by every GPU that loads the library until the process exits.
 //
 // Host code may not pass the array's name to a kernel: on the host it is a stand-in symbol,
 // not a device address.  The device address is looked up once per device with

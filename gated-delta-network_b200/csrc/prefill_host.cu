@@ -113,9 +113,12 @@ bool build_prefill_maps(const PrefillArgs& p, int bv, PrefillMaps* m) {
     ok = ok && map3d(&m->v, p.v, BF, 128, kHV, T, 256, 256 * kHV, 64, 1, 64, SW);
     // Workspace: [8][R][cols] as (col, row, head); one box = one 64-row chunk slot.
     ok = ok && map3d(&m->w, p.w, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
-    ok = ok && map3d(&m->aqk, p.aqk, BF, 64, R, kHV, 128, R * 128, 64, 64, 1, SW);
+    ok = ok && map3d(&m->qp, p.qp, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
+    ok = ok && map3d(&m->oi, p.oi, BF, 128, R, kHV, 256, R * 256, (uint32_t)bv, 64, 1, NS);
     ok = ok && map3d(&m->u, p.u, F32, 128, R, kHV, 512, R * 512, (uint32_t)bv, 64, 1, NS);
     ok = ok && map3d(&m->g4, p.g4, F32, 4, R, kHV, 16, R * 16, 4, 64, 1, NS);
+    ok = ok && map3d(&m->u_st, p.u, F32, 128, R, kHV, 512, R * 512, 32, 64, 1, SW);
+    ok = ok && map3d(&m->oi_st, p.oi, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
     return ok;
 }
 

@@ -16,9 +16,12 @@ struct PrefillMaps {
     CUtensorMap k;    // same
     CUtensorMap v;    // (128, 8, T) bf16, box 64 x 1 x 64, SWIZZLE_128B
     CUtensorMap w;    // (128 col, S*64 row, 8 head) bf16, box 64 x 64 x 1, SWIZZLE_128B
-    CUtensorMap aqk;  // (64, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B
+    CUtensorMap qp;   // (128, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B
+    CUtensorMap oi;   // (128, S*64, 8) bf16, box BV x 64 x 1, no swizzle
     CUtensorMap u;    // (128, S*64, 8) f32, box BV x 64 x 1, no swizzle
     CUtensorMap g4;   // (4, S*64, 8) f32, box 4 x 64 x 1, no swizzle
+    CUtensorMap u_st;   // (128, S*64, 8) f32, box 32 x 64 x 1, SWIZZLE_128B (prep's stores)
+    CUtensorMap oi_st;  // (128, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B (prep's stores)
 };
 
 // Sequence n's token range [s, e), clamped to [0, T] (malformed cu_seqlens cannot index outside).

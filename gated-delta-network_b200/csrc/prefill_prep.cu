@@ -12,14 +12,21 @@
 //   * TMA (SWIZZLE_128B boxes, no multicast) brings K, Q (qk head) and V (v-head) tiles.
 //   * tcgen05 MMA #1 (M=128, N=64, K=128): [K; Q] x K^T -> TMEM, rows 0-63 K K^T, 64-127 Q K^T.
 //   * Epilogue: one thread per TMEM lane turns its row into a row of A (fp32, shared memory)
-//     or of Aqk (bf16, global).
+//     or of Aqk (bf16, shared memory, operand of MMA #3).
 //   * T = (I + A)^-1: 16x16 diagonal blocks by forward substitution (one column per lane),
 //     off-diagonal blocks T_ib,jb = -T_ib,ib sum_k A_ib,k T_k,jb with tf32 mma.sync.
 //   * tcgen05 MMA #2 (M=128, N=256, K=64): [T diag(beta e^G); (T - I) diag(beta)] x [K | V]
 //     -> TMEM; rows 0-63 / columns 0-127 are w, rows 64-127 / columns 128-255 are u - beta v.
-//   * Outputs go to the chunk's workspace slot; rows past the chunk end are written as zeros.
+//   * tcgen05 MMA #3 (M=128, N=256, K=64): [Aqk; Aqk] x [w | u] -> TMEM; rows 0-63 / columns
+//     0-127 are Aqk w, rows 64-127 / columns 128-255 are Aqk u.  They give the chunk's output
+//     operands Q' = diag(e^G) Q - Aqk w and oi = Aqk u, so the serial scan needs only
+//     o = scale (Q' h + oi) (the Aqk (u - w h) term of chunk_o, fla_kernels.py:758-796).
+//   * Outputs go to the chunk's workspace slot; rows past the chunk end carry zero / finite padding.
 #include "prefill_kernels.cuh"
 #include "sm100.cuh"
+#include "dbg.cuh"
+
+GDN_DBG_READER(gdn_debug_read_prep)
 
 namespace gdn {
 namespace prep2 {
@@ -34,14 +41,16 @@ constexpr uint32_t kOffMisc = 40960;  // 8 KB: scratch, gates, barriers
 constexpr uint32_t kOffV1 = 49152;    // V cols 64-127
 constexpr uint32_t kOffA = 57344;     // A fp32 [64][68]; later [Wb; Ub] bf16 [128][64] SW128
 constexpr uint32_t kOffT = kOffA + 64 * kFS * 4;  // T fp32 [64][68]
-constexpr uint32_t kSmemUsed = kOffT + 64 * kFS * 4;
+constexpr uint32_t kOffAq = kOffT + 64 * kFS * 4;  // [Aqk; Aqk] bf16 [128][64] SW128 (1024-aligned)
+constexpr uint32_t kSmemUsed = kOffAq + 16384;
 constexpr uint32_t kSmem = kSmemUsed + 1024;  // slack for 1024-byte alignment
 // inside the misc block
 constexpr uint32_t kOffY = 0;                  // [4 warps][16][17] f32
 constexpr uint32_t kOffG = kOffY + 4 * 16 * 17 * 4;
 constexpr uint32_t kOffB = kOffG + 64 * 4;
 constexpr uint32_t kOffE = kOffB + 64 * 4;
-constexpr uint32_t kOffBar = kOffE + 64 * 4;   // 2 mbarriers
+constexpr uint32_t kOffGf = kOffE + 64 * 4;    // [64] f32 final cumulative log decay
+constexpr uint32_t kOffBar = kOffGf + 64 * 4;  // 2 mbarriers
 constexpr uint32_t kOffSlot = kOffBar + 16;
 static_assert(kOffSlot + 16 <= 8192, "misc block");
 constexpr uint32_t kTmemCols = 256;
@@ -73,6 +82,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     float* Gs = reinterpret_cast<float*>(misc + kOffG);
     float* Bs = reinterpret_cast<float*>(misc + kOffB);
     float* Es = reinterpret_cast<float*>(misc + kOffE);
+    float* Gf = reinterpret_cast<float*>(misc + kOffGf);
     uint64_t* bar_load = reinterpret_cast<uint64_t*>(misc + kOffBar);
     uint64_t* bar_mma = bar_load + 1;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(misc + kOffSlot);
@@ -87,6 +97,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     const int bos = s0 + (slot - p.chunk_base[seq]) * kChunk;
     const int L = min(kChunk, e0 - bos);
     const size_t row0 = (size_t)hv * p.S * kChunk + (size_t)slot * kChunk;  // workspace row of token bos
+    long long tp = clock64();
+    const bool dbg = true;
+    (void)dbg;
 
     // ---- 1. barriers, TMA loads, TMEM, gates ------------------------------------------------
     if (tid == 0) {
@@ -127,17 +140,18 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    // Gs holds per-warp prefix sums; the chunk prefix adds warp 0's total to tokens 32..63.
+    // Padded tokens (t >= L) carry g = 0, so their cumulative G repeats G_{L-1}.
     if (tid < 64) {
-        // padded tokens (t >= L) carry g = 0, so their cumulative G repeats G_{L-1}
-        float x = Gs[tid];
-        if (tid >= 32) x += Gs[31];
+        const float x = Gs[tid] + (tid >= 32 ? Gs[31] : 0.f);
+        Gf[tid] = x;
         Es[tid] = __expf(x);
-        Gs[tid] = x;  // warp 0 rewrites Gs[0..31] unchanged; warp 1 only reads Gs[31]
     }
     bool ok = mbar_wait(bar_load, 0, p.status, kErrPrepTmaTimeout);
-    ok = __syncthreads_and(ok);  // also publishes Gs / Es
+    ok = __syncthreads_and(ok);  // also publishes Gf / Es
     if (!ok) goto cleanup;
 
+    GDN_PH_ACC(dbg, 0, tp);
     // ---- 2. MMA #1: [K; Q] (128 x 128) x K^T -> TMEM columns 0..63 ---------------------------
     if (tid == 0) {
         tc_fence_after();
@@ -155,14 +169,31 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     if (!ok) goto cleanup;
     tc_fence_after();
 
+    GDN_PH_ACC(dbg, 1, tp);
     // ---- 3. epilogue #1: thread r owns TMEM lane r (rows 0-63: K K^T, rows 64-127: Q K^T) -----
     {
         const int r = tid, i = r & 63;
         const bool qk = r >= 64;
-        const float Gi = Gs[i], bi = Bs[i];
+        const float Gi = Gf[i], bi = Bs[i];
         const bool live = i < L;
+        auto decay = [&](int j) -> float { return __expf(Gi - Gf[j]); };  // only formed for j <= i
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
+            if (half == 1 && (warp & 1) == 0) {
+                // rows 0..31: columns 32..63 lie above the diagonal.  A's upper triangle is never
+                // read; the Aqk operand needs explicit zeros there.
+                if (qk) {
+#pragma unroll
+                    for (int j8 = 0; j8 < 4; ++j8) {
+                        const uint32_t ch = (uint32_t)(4 + j8);
+                        *reinterpret_cast<uint4*>(sm + kOffAq + i * 128 + ((ch ^ (uint32_t)(i & 7)) << 4)) =
+                            make_uint4(0, 0, 0, 0);
+                        *reinterpret_cast<uint4*>(sm + kOffAq + (64 + i) * 128 + ((ch ^ (uint32_t)(i & 7)) << 4)) =
+                            make_uint4(0, 0, 0, 0);
+                    }
+                }
+                continue;
+            }
             float d[32];
             tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 32 * half, d);
             if (!qk) {
@@ -173,31 +204,34 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int j = 32 * half + 4 * j4 + e;
-                        po[e] = (live && j < i) ? bi * __expf(Gi - Gs[j]) * d[4 * j4 + e] : 0.f;
+                        po[e] = (live && j < i) ? bi * decay(j) * d[4 * j4 + e] : 0.f;
                     }
                     *reinterpret_cast<float4*>(Af + i * kFS + 32 * half + 4 * j4) = o;
                 }
             } else {
-                uint16_t* dst = p.aqk + (row0 + i) * 64 + 32 * half;
 #pragma unroll
                 for (int j8 = 0; j8 < 4; ++j8) {
                     uint32_t pk[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int j0 = 32 * half + 8 * j8 + 2 * e;
-                        const float x0 = (live && j0 <= i) ? __expf(Gi - Gs[j0]) * d[8 * j8 + 2 * e] : 0.f;
-                        const float x1 = (live && j0 + 1 <= i) ? __expf(Gi - Gs[j0 + 1]) * d[8 * j8 + 2 * e + 1] : 0.f;
+                        const float x0 = (live && j0 <= i) ? decay(j0) * d[8 * j8 + 2 * e] : 0.f;
+                        const float x1 = (live && j0 + 1 <= i) ? decay(j0 + 1) * d[8 * j8 + 2 * e + 1] : 0.f;
                         pk[e] = pack_bf16x2(x0, x1);
                     }
-                    *reinterpret_cast<uint4*>(dst + 8 * j8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    const uint4 q4 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    const uint32_t ch = (uint32_t)(4 * half + j8);
+                    *reinterpret_cast<uint4*>(sm + kOffAq + i * 128 + ((ch ^ (uint32_t)(i & 7)) << 4)) = q4;
+                    *reinterpret_cast<uint4*>(sm + kOffAq + (64 + i) * 128 + ((ch ^ (uint32_t)(i & 7)) << 4)) = q4;
                 }
             }
         }
-        if (tid < 64) *reinterpret_cast<float4*>(p.g4 + (row0 + tid) * 4) = make_float4(Gs[tid], Es[tid], Bs[tid], 0.f);
+        if (tid < 64) *reinterpret_cast<float4*>(p.g4 + (row0 + tid) * 4) = make_float4(Gf[tid], Es[tid], Bs[tid], 0.f);
     }
     tc_fence_before();
     __syncthreads();
 
+    GDN_PH_ACC(dbg, 2, tp);
     // ---- 4. T = (I + A)^-1 ----------------------------------------------------------------
     // 4a. diagonal 16x16 blocks: warp w inverts block w, lanes 0..15 each own one column.
     {
@@ -272,6 +306,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     }
     __syncthreads();
 
+    GDN_PH_ACC(dbg, 3, tp);
     // ---- 5. MMA #2 operand [T diag(beta e^G); (T - I) diag(beta)]: bf16 [128][64] SW128 -----
     {
         const int r = tid, m = r & 63;
@@ -301,6 +336,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     tc_fence_before();
     __syncthreads();
 
+    GDN_PH_ACC(dbg, 4, tp);
     // ---- 6. MMA #2: [Wb; Ub] (128 x 64) x [K | V] (64 x 256, N-major) -> TMEM columns 0..255 --
     if (tid == 0) {
         tc_fence_after();
@@ -316,27 +352,30 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     if (!ok) goto cleanup;
     tc_fence_after();
 
+    GDN_PH_ACC(dbg, 5, tp);
     // ---- 7. epilogue #2: rows 0-63 -> w (bf16), rows 64-127 -> u = D + beta v (f32) ---------
     {
         const int r = tid;
         const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
         if (r < 64) {
-            uint16_t* dst = p.w + (row0 + r) * kD;
+            // w row r -> the (now free) K tile: MMA #3's B operand and the TMA store's source
 #pragma unroll 1
             for (int cb = 0; cb < 4; ++cb) {
                 float d[32];
                 tmem_ld32(tl + 32 * cb, d);
 #pragma unroll
-                for (int j8 = 0; j8 < 4; ++j8)
-                    *reinterpret_cast<uint4*>(dst + 32 * cb + 8 * j8) =
+                for (int j8 = 0; j8 < 4; ++j8) {
+                    const uint4 w4 =
                         make_uint4(pack_bf16x2(d[8 * j8], d[8 * j8 + 1]), pack_bf16x2(d[8 * j8 + 2], d[8 * j8 + 3]),
                                    pack_bf16x2(d[8 * j8 + 4], d[8 * j8 + 5]), pack_bf16x2(d[8 * j8 + 6], d[8 * j8 + 7]));
+                    *reinterpret_cast<uint4*>(sm + kOffK0 + sw128_off(r, 32 * cb + 8 * j8, kOffK1 - kOffK0)) = w4;
+                }
             }
         } else {
             const int m = r - 64;
             const float be = Bs[m];
-            float* dst = p.u + (row0 + m) * kD;
-            const unsigned char* vt = sm + kOffV0;
+            unsigned char* ust = sm + kOffA;  // f32 staging tile of u (4 SW128 atoms of 32 columns)
+            unsigned char* vt = sm + kOffV0;
 #pragma unroll 1
             for (int cb = 0; cb < 4; ++cb) {
                 float d[32];
@@ -344,19 +383,95 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
                     const int c = 32 * cb + 4 * j4;
-                    const uint2 vv = *reinterpret_cast<const uint2*>(vt + sw128_off(m, c, kOffV1 - kOffV0));
+                    uint2* vp = reinterpret_cast<uint2*>(vt + sw128_off(m, c, kOffV1 - kOffV0));
+                    const uint2 vv = *vp;
                     float4 o;
                     o.x = fmaf(be, __uint_as_float(vv.x << 16), d[4 * j4 + 0]);
                     o.y = fmaf(be, __uint_as_float(vv.x & 0xffff0000u), d[4 * j4 + 1]);
                     o.z = fmaf(be, __uint_as_float(vv.y << 16), d[4 * j4 + 2]);
                     o.w = fmaf(be, __uint_as_float(vv.y & 0xffff0000u), d[4 * j4 + 3]);
-                    *reinterpret_cast<float4*>(dst + c) = o;
+                    *reinterpret_cast<float4*>(ust + sw128_off_f32(m, c, 8192)) = o;
+                    // u (bf16) replaces this thread's own V row in place: MMA #3's B operand
+                    *vp = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
                 }
             }
         }
     }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    GDN_PH_ACC(dbg, 6, tp);
+    // ---- 8. MMA #3: [Aqk; Aqk] (128 x 64) x [w | u] (64 x 256, N-major) -> TMEM columns 0..255 --
+    if (tid == 0) {
+        const int wr = slot * kChunk;
+        tma_store_3d(&maps.w, 0, wr, hv, sm + kOffK0);
+        tma_store_3d(&maps.w, 64, wr, hv, sm + kOffK1);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) tma_store_3d(&maps.u_st, 32 * a, wr, hv, sm + kOffA + 8192 * a);
+        tma_store_commit();
+        tc_fence_after();
+        constexpr uint32_t idesc = umma_idesc_bf16(128, 256, false, true);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem, umma_desc_sw128(sbase + kOffAq + 32u * kk, 16, 1024),
+                      umma_desc_sw128(sbase + kOffK0 + 2048u * kk, kOffK1 - kOffK0, 1024), idesc, kk > 0);
+        umma_commit(bar_mma);
+    }
+    ok = mbar_wait(bar_mma, 0, p.status, kErrPrepMmaTimeout);
+    if (tid == 0) tma_store_wait_read();  // the w store has read the K tile: it can be overwritten
+    ok = __syncthreads_and(ok);
+    if (!ok) goto cleanup;
+    tc_fence_after();
+
+    GDN_PH_ACC(dbg, 7, tp);
+    // ---- 9. epilogue #3: rows 0-63 -> Q' = e^G q - Aqk w, rows 64-127 -> oi = Aqk u (bf16) --------
+    {
+        const int r = tid;
+        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+        const int m = r & 63;
+        const float eg = Es[m];
+        unsigned char* dst = sm + (r < 64 ? kOffK0 : kOffV0);  // Q' -> K tile, oi -> V tile (SW128)
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+            float d[32];
+            tmem_ld32(tl + (r < 64 ? 0 : 128) + 32 * cb, d);
+#pragma unroll
+            for (int j8 = 0; j8 < 4; ++j8) {
+                const int c = 32 * cb + 8 * j8;
+                float x[8];
+                if (r < 64) {
+                    const uint4 q4 = *reinterpret_cast<const uint4*>(sm + kOffQ0 + sw128_off(m, c, kOffQ1 - kOffQ0));
+                    const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        x[2 * e] = fmaf(eg, __uint_as_float(qw[e] << 16), -d[8 * j8 + 2 * e]);
+                        x[2 * e + 1] = fmaf(eg, __uint_as_float(qw[e] & 0xffff0000u), -d[8 * j8 + 2 * e + 1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) x[e] = d[8 * j8 + e];
+                }
+                *reinterpret_cast<uint4*>(dst + sw128_off(m, c, kOffK1 - kOffK0)) =
+                    make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                               pack_bf16x2(x[6], x[7]));
+            }
+        }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        const int wr = slot * kChunk;
+        tma_store_3d(&maps.qp, 0, wr, hv, sm + kOffK0);
+        tma_store_3d(&maps.qp, 64, wr, hv, sm + kOffK1);
+        tma_store_3d(&maps.oi_st, 0, wr, hv, sm + kOffV0);
+        tma_store_3d(&maps.oi_st, 64, wr, hv, sm + kOffV1);
+        tma_store_commit();
+    }
 
 cleanup:
+    if (tid == 0) tma_store_wait_all();  // shared memory must outlive the stores that read it
+    GDN_PH_ACC(dbg, 8, tp);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, kTmemCols);

@@ -6,37 +6,41 @@
 // solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/fla_kernels.py:411-671 chunk_h
 // and 714-796 chunk_o; the per-chunk state snapshots never leave the SM):
 //   vn = u - w h                                  (u, w from the prep kernel's workspace slot)
-//   o  = scale (e^G . (Q h) + Aqk vn)             -> out
+//   o  = scale (Q' h + oi)                        -> out   (Q' = e^G.Q - Aqk w, oi = Aqk u, so
+//                                                  o = scale (e^G.(Q h) + Aqk vn) as in chunk_o)
 //   h  = e^{G_last} h + K^T (e^{G_last - G} . vn) (vn split into bf16 hi + lo: ~16-bit mantissa)
-// Each chunk's W, Q, K, Aqk (SWIZZLE_128B), u slice and G tiles arrive by TMA (one thread
-// issues them) into a 3-stage ring of shared-memory buffers tracked by mbarriers, two chunks
-// ahead of the math.  The serial dependency (w h -> vn -> K^T vn -> h) uses warp-level
+// Each chunk's W, Q', K (SWIZZLE_128B), u / oi slices and G tiles arrive by TMA into a 3-stage
+// ring of shared-memory buffers: a producer warp issues the copies as soon as the four math
+// warps release a stage (empty / full mbarrier pairs), so the math never waits on TMA issue.  The serial dependency (w h -> vn -> K^T vn -> h) uses warp-level
 // mma.sync fragments: their ~20-cycle latency beats a tcgen05 round trip (~570 cycles) for
 // these 64 x BV x 128 products, and the state never has to leave the register file.
 #include "prefill_kernels.cuh"
 #include "sm100.cuh"
+#include "dbg.cuh"
+
+GDN_DBG_READER(gdn_debug_read_scan)
 
 namespace gdn {
 
 template <int BV>
 struct Scan2Cfg {
-    static constexpr int kThreads = 128;
+    static constexpr int kThreads = 160;    // 4 math warps + 1 TMA producer warp
+    static constexpr int kMath = 128;
     static constexpr int kStages = 3;
     static constexpr int kHS = BV + 8;  // bf16 row stride of the [rows][BV] operand tiles
     static constexpr uint32_t kOffW = 0;        // 2 atoms of 64 rows x 128 B (atom stride 8 KB)
     static constexpr uint32_t kOffQ = 16384;
     static constexpr uint32_t kOffK = 32768;
-    static constexpr uint32_t kOffA = 49152;    // Aqk: 1 atom
-    static constexpr uint32_t kOffU = 57344;    // [64][BV] f32
-    static constexpr uint32_t kOffG = kOffU + 64 * BV * 4;  // [64][4] f32 {G, e^G, beta, 0}
+    static constexpr uint32_t kOffU = 49152;                // [64][BV] f32
+    static constexpr uint32_t kOffO = kOffU + 64 * BV * 4;  // [64][BV] bf16 (oi)
+    static constexpr uint32_t kOffG = kOffO + 64 * BV * 2;  // [64][4] f32 {G, e^G, beta, 0}
     static constexpr uint32_t kStage = ((kOffG + 1024) + 1023) & ~1023u;
-    static constexpr uint32_t kTxBytes = 3 * 16384 + 8192 + 64 * BV * 4 + 1024;
+    static constexpr uint32_t kTxBytes = 3 * 16384 + 64 * BV * 6 + 1024;
     static constexpr uint32_t kOffHb = kStages * kStage;               // [128][kHS] bf16
-    static constexpr uint32_t kOffVn = kOffHb + 128 * kHS * 2;          // [64][kHS] bf16
-    static constexpr uint32_t kOffVh = kOffVn + 64 * kHS * 2;
+    static constexpr uint32_t kOffVh = kOffHb + 128 * kHS * 2;          // [64][kHS] bf16
     static constexpr uint32_t kOffVl = kOffVh + 64 * kHS * 2;
     static constexpr uint32_t kOffBar = (kOffVl + 64 * kHS * 2 + 15) & ~15u;
-    static constexpr uint32_t kSmemUsed = kOffBar + 8 * kStages;
+    static constexpr uint32_t kSmemUsed = kOffBar + 16 * kStages + 16;  // full[], empty[], abort flag
     static constexpr uint32_t kSmem = kSmemUsed + 1024;
     static_assert(kSmem <= 227 * 1024, "scan shared memory");
 };
@@ -59,7 +63,7 @@ __device__ __forceinline__ void load_b_frags(uint32_t (&b)[NT8][2], const uint16
 }
 
 template <int BV>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(160, 1)
     gdn_prefill_scan2_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using C = Scan2Cfg<BV>;
     constexpr int NT8 = BV / 8;
@@ -67,10 +71,11 @@ __global__ void __launch_bounds__(128, 1)
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint16_t* Hb = reinterpret_cast<uint16_t*>(sm + C::kOffHb);
-    uint16_t* VNb = reinterpret_cast<uint16_t*>(sm + C::kOffVn);
     uint16_t* VNh = reinterpret_cast<uint16_t*>(sm + C::kOffVh);
     uint16_t* VNl = reinterpret_cast<uint16_t*>(sm + C::kOffVl);
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
+    uint64_t* empty = full + C::kStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;
@@ -108,21 +113,41 @@ __global__ void __launch_bounds__(128, 1)
         mbar_arrive_expect_tx(bar, C::kTxBytes);
         tma_load_3d(st + C::kOffW, &maps.w, 0, wr, hv, bar);
         tma_load_3d(st + C::kOffW + 8192, &maps.w, 64, wr, hv, bar);
-        tma_load_3d(st + C::kOffQ, &maps.q, 0, hq, t0, bar);
-        tma_load_3d(st + C::kOffQ + 8192, &maps.q, 64, hq, t0, bar);
+        tma_load_3d(st + C::kOffQ, &maps.qp, 0, wr, hv, bar);
+        tma_load_3d(st + C::kOffQ + 8192, &maps.qp, 64, wr, hv, bar);
         tma_load_3d(st + C::kOffK, &maps.k, 0, hq, t0, bar);
         tma_load_3d(st + C::kOffK + 8192, &maps.k, 64, hq, t0, bar);
-        tma_load_3d(st + C::kOffA, &maps.aqk, 0, wr, hv, bar);
         tma_load_3d(st + C::kOffU, &maps.u, v0, wr, hv, bar);
+        tma_load_3d(st + C::kOffO, &maps.oi, v0, wr, hv, bar);
         tma_load_3d(st + C::kOffG, &maps.g4, 0, wr, hv, bar);
     };
     if (tid == 0) {
-        for (int s = 0; s < C::kStages; ++s) mbar_init(full + s, 1);
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, C::kMath / 32);
+        }
+        *abort_flag = 0;
         mbar_fence_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        for (int c = 0; c < min(nchunks, C::kStages - 1); ++c) issue(c);
+    if (warp == C::kMath / 32) {
+        // Producer: refill stage c % 3 with chunk c once the math warps released chunk c - 3.
+        if (lane == 0) {
+            tma_prefetch_desc(&maps.w);
+            tma_prefetch_desc(&maps.qp);
+            tma_prefetch_desc(&maps.k);
+            tma_prefetch_desc(&maps.oi);
+            tma_prefetch_desc(&maps.u);
+            tma_prefetch_desc(&maps.g4);
+            for (int c = 0; c < nchunks; ++c) {
+                if (c >= C::kStages &&
+                    !mbar_wait(empty + (c % C::kStages), (uint32_t)((c / C::kStages - 1) & 1), p.status,
+                               kErrScanTmaTimeout))
+                    break;  // the math warps stopped; they also stop waiting for more chunks
+                issue(c);
+            }
+        }
+        return;
     }
 
     // state slice h[kdim][v] as mma C fragments: rows 32*warp + 16*mt + gq (+8), cols 8*nt + 2*tq (+1)
@@ -153,22 +178,23 @@ __global__ void __launch_bounds__(128, 1)
                 }
     };
     write_hb();
+    named_bar_sync(1, C::kMath);
 
+    const bool dbg = blockIdx.x == 0 && blockIdx.y == 0;
+    long long tp = clock64();
+    (void)dbg;
     int c = 0;
     for (; c < nchunks; ++c) {
-        // The buffers of stage (c+2) % 3 were last read in chunk c-1, which every thread has
-        // finished (barrier at the end of the previous iteration): refill them with chunk c+2.
-        if (tid == 0 && c + C::kStages - 1 < nchunks) issue(c + C::kStages - 1);
-        bool ok = mbar_wait(full + (c % C::kStages), (uint32_t)((c / C::kStages) & 1), p.status, kErrScanTmaTimeout);
-        ok = __syncthreads_and(ok);  // also orders the previous iteration's Hb writes
-        if (!ok) break;
+        if (!mbar_wait(full + (c % C::kStages), (uint32_t)((c / C::kStages) & 1), p.status, kErrScanTmaTimeout))
+            *abort_flag = 1;  // checked by every math thread after the next barrier
+        GDN_PH_ACC(dbg, 20, tp);
 
         const unsigned char* st = sm + (c % C::kStages) * C::kStage;
         const unsigned char* Ws = st + C::kOffW;
         const unsigned char* Qs = st + C::kOffQ;
         const unsigned char* Ks = st + C::kOffK;
-        const unsigned char* As = st + C::kOffA;
         const float* Us = reinterpret_cast<const float*>(st + C::kOffU);
+        const uint16_t* Os = reinterpret_cast<const uint16_t*>(st + C::kOffO);
         const float* G4 = reinterpret_cast<const float*>(st + C::kOffG);
         const int t0 = bos + c * kChunk;
         const int L = min(kChunk, eos - t0);
@@ -193,59 +219,37 @@ __global__ void __launch_bounds__(128, 1)
                 mma_bf16(p2[nt], aq, b[nt][0], b[nt][1]);
             }
         }
-        // (2) vn = u - P1; o = scale e^G P2; stage vn (bf16) and the decayed vn (hi + lo)
-        float o[NT8][4];
+        GDN_PH_ACC(dbg, 21, tp);
+        // (2) vn = u - P1 -> decayed vn (hi + lo) for the state update; o = scale (P2 + oi) -> out
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
             const int row = 16 * warp + gq + 8 * half;
-            const float eg = G4[row * 4 + 1];
             const float ed = __expf(GL - G4[row * 4]);  // <= 1; padded rows have vn = 0
+            uint16_t* dst = p.out + ((size_t)(t0 + row) * kHV + hv) * kD + v0;
 #pragma unroll
             for (int nt = 0; nt < NT8; ++nt) {
                 const int col = 8 * nt + 2 * tq;
                 const float2 uu = *reinterpret_cast<const float2*>(Us + row * BV + col);
                 const float vn0 = uu.x - p1[nt][2 * half];
                 const float vn1 = uu.y - p1[nt][2 * half + 1];
-                o[nt][2 * half] = p.scale * eg * p2[nt][2 * half];
-                o[nt][2 * half + 1] = p.scale * eg * p2[nt][2 * half + 1];
-                *reinterpret_cast<uint32_t*>(VNb + row * HS + col) = pack_bf16x2(vn0, vn1);
                 const float d0 = vn0 * ed, d1 = vn1 * ed;
                 const uint32_t hi = pack_bf16x2(d0, d1);
                 *reinterpret_cast<uint32_t*>(VNh + row * HS + col) = hi;
                 *reinterpret_cast<uint32_t*>(VNl + row * HS + col) =
                     pack_bf16x2(d0 - __uint_as_float(hi << 16), d1 - __uint_as_float(hi & 0xffff0000u));
-            }
-        }
-        __syncthreads();
-
-        // (3a) o += scale Aqk vn; store the chunk's outputs
-        {
-            float acc[NT8][4];
-#pragma unroll
-            for (int nt = 0; nt < NT8; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-#pragma unroll
-            for (int k0 = 0; k0 < 64; k0 += 16) {
-                uint32_t a[4], b[NT8][2];
-                ldsm_x4(a[0], a[1], a[2], a[3], As + sw128_off(16 * warp + (lane & 15), k0 + ((lane >> 4) << 3), 0));
-                load_b_frags<NT8, HS>(b, VNb, k0, lane);
-#pragma unroll
-                for (int nt = 0; nt < NT8; ++nt) mma_bf16(acc[nt], a, b[nt][0], b[nt][1]);
-            }
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int row = 16 * warp + gq + 8 * half;
                 if (row < L) {
-                    uint16_t* dst = p.out + ((size_t)(t0 + row) * kHV + hv) * kD + v0;
-#pragma unroll
-                    for (int nt = 0; nt < NT8; ++nt)
-                        *reinterpret_cast<uint32_t*>(dst + 8 * nt + 2 * tq) =
-                            pack_bf16x2(fmaf(p.scale, acc[nt][2 * half], o[nt][2 * half]),
-                                        fmaf(p.scale, acc[nt][2 * half + 1], o[nt][2 * half + 1]));
+                    const uint32_t oo = *reinterpret_cast<const uint32_t*>(Os + row * BV + col);
+                    *reinterpret_cast<uint32_t*>(dst + col) =
+                        pack_bf16x2(p.scale * (p2[nt][2 * half] + __uint_as_float(oo << 16)),
+                                    p.scale * (p2[nt][2 * half + 1] + __uint_as_float(oo & 0xffff0000u)));
                 }
             }
         }
+        GDN_PH_ACC(dbg, 22, tp);
+        named_bar_sync(1, C::kMath);
+        GDN_PH_ACC(dbg, 23, tp);
+        if (*abort_flag) break;  // written only before this barrier: every math thread sees the same value
+
         // (3b) h = e^{GL} h + K^T (vn_hi + vn_lo)   (rows 32*warp .. +31 of the K dimension)
         {
             const float eL = __expf(GL);
@@ -274,11 +278,15 @@ __global__ void __launch_bounds__(128, 1)
                     }
             }
         }
+        GDN_PH_ACC(dbg, 24, tp);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + (c % C::kStages));  // this warp is done with the stage
         write_hb();
-        __syncthreads();
+        named_bar_sync(1, C::kMath);
+        GDN_PH_ACC(dbg, 25, tp);
     }
     if (c < nchunks) {
-        // A TMA wait gave up: let the copies already issued land (bounded) before the CTA exits.
+        // A TMA wait gave up: let copies already in flight land (bounded) before the CTA exits.
         if (tid == 0)
             for (int cc = c + 1; cc < min(nchunks, c + C::kStages); ++cc)
                 mbar_wait(full + (cc % C::kStages), (uint32_t)((cc / C::kStages) & 1), nullptr, 0);

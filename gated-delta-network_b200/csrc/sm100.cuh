@@ -35,6 +35,13 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Barrier among the first `nthreads` threads of the CTA (named barrier `id`, 1..15).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -65,6 +72,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
+// TMA tensor tile store (shared -> global), tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int x, int y, int z, const void* src) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the committed stores have finished reading shared memory.
+__device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until the committed stores are complete (written to global memory).
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -75,6 +94,13 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 __device__ __forceinline__ uint32_t sw128_off(int r, int c, uint32_t atom_stride) {
     return (uint32_t)(c >> 6) * atom_stride + (uint32_t)r * 128u + ((((uint32_t)(c >> 3) & 7u) ^ ((uint32_t)r & 7u)) << 4) +
            (uint32_t)(c & 7) * 2u;
+}
+
+// Byte offset of element (r, c) of a [rows][128] f32 tile stored as four 32-column
+// SWIZZLE_128B atoms (atom a = c / 32 holds rows x 128 B) of `atom_stride` bytes each.
+__device__ __forceinline__ uint32_t sw128_off_f32(int r, int c, uint32_t atom_stride) {
+    return (uint32_t)(c >> 5) * atom_stride + (uint32_t)r * 128u + ((((uint32_t)(c >> 2) & 7u) ^ ((uint32_t)r & 7u)) << 4) +
+           (uint32_t)(c & 3) * 4u;
 }
 
 // ---- tcgen05 / TMEM -------------------------------------------------------------------------

@@ -18,7 +18,7 @@ INCLUDE = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200.so")
 SOURCES = ["api.cu", "decode.cu", "prefill_host.cu", "prefill_prep.cu", "prefill_scan.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "kernels.cuh", "sm100.cuh", "prefill_kernels.cuh"]
+HEADERS = ["common.cuh", "kernels.cuh", "sm100.cuh", "prefill_kernels.cuh", "dbg.cuh"]
 
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",
