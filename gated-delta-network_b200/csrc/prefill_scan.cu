@@ -10,10 +10,13 @@
 //                                                  o = scale (e^G.(Q h) + Aqk vn) as in chunk_o)
 //   h  = e^{G_last} h + K^T (e^{G_last - G} . vn) (vn split into bf16 hi + lo: ~16-bit mantissa)
 // Each chunk's W, Q', K (SWIZZLE_128B), u / oi slices and G tiles arrive by TMA into a 3-stage
-// ring of shared-memory buffers: a producer warp issues the copies as soon as the four math
-// warps release a stage (empty / full mbarrier pairs), so the math never waits on TMA issue.  The serial dependency (w h -> vn -> K^T vn -> h) uses warp-level
-// mma.sync fragments: their ~20-cycle latency beats a tcgen05 round trip (~570 cycles) for
-// these 64 x BV x 128 products, and the state never has to leave the register file.
+// ring of shared-memory buffers: a producer warp issues the copies as soon as the math warps
+// release a stage (empty / full mbarrier pairs), so the math never waits on TMA issue.
+// Eight math warps (two per SM sub-partition) split every phase: warps 0-3 form w h and vn
+// while warps 4-7 form Q' h and the outputs; all eight update 16 state rows each.  The serial
+// dependency (w h -> vn -> K^T vn -> h) uses warp-level mma.sync fragments: their ~20-cycle
+// latency beats a tcgen05 round trip (~570 cycles) for these 64 x BV x 128 products, and the
+// state never leaves the register file.
 #include "prefill_kernels.cuh"
 #include "sm100.cuh"
 #include "dbg.cuh"
@@ -24,10 +27,12 @@ namespace gdn {
 
 template <int BV>
 struct Scan2Cfg {
-    static constexpr int kThreads = 160;    // 4 math warps + 1 TMA producer warp
-    static constexpr int kMath = 128;
+    static constexpr int kThreads = 288;    // 8 math warps + 1 TMA producer warp
+    static constexpr int kMath = 256;
     static constexpr int kStages = 3;
-    static constexpr int kHS = BV + 8;  // bf16 row stride of the [rows][BV] operand tiles
+    // bf16 row stride of the [rows][BV] operand tiles: 8 consecutive rows must start in 8
+    // different 16-byte bank groups for conflict-free ldmatrix (16 B for BV=8, 48 B, 80 B).
+    static constexpr int kHS = BV == 8 ? 8 : BV + 8;
     static constexpr uint32_t kOffW = 0;        // 2 atoms of 64 rows x 128 B (atom stride 8 KB)
     static constexpr uint32_t kOffQ = 16384;
     static constexpr uint32_t kOffK = 32768;
@@ -62,12 +67,14 @@ __device__ __forceinline__ void load_b_frags(uint32_t (&b)[NT8][2], const uint16
     }
 }
 
+
 template <int BV>
-__global__ void __launch_bounds__(160, 1)
+__global__ void __launch_bounds__(288, 1)
     gdn_prefill_scan2_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using C = Scan2Cfg<BV>;
     constexpr int NT8 = BV / 8;
     constexpr int HS = C::kHS;
+    constexpr int kMathWarps = C::kMath / 32;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint16_t* Hb = reinterpret_cast<uint16_t*>(sm + C::kOffHb);
@@ -106,92 +113,86 @@ __global__ void __launch_bounds__(160, 1)
     const int nchunks = (len + kChunk - 1) / kChunk;
     const int slot0 = p.chunk_base[n];
 
-    auto issue = [&](int c) {
-        unsigned char* st = sm + (c % C::kStages) * C::kStage;
-        uint64_t* bar = full + (c % C::kStages);
-        const int slot = slot0 + c, t0 = bos + c * kChunk, wr = slot * kChunk;
-        mbar_arrive_expect_tx(bar, C::kTxBytes);
-        tma_load_3d(st + C::kOffW, &maps.w, 0, wr, hv, bar);
-        tma_load_3d(st + C::kOffW + 8192, &maps.w, 64, wr, hv, bar);
-        tma_load_3d(st + C::kOffQ, &maps.qp, 0, wr, hv, bar);
-        tma_load_3d(st + C::kOffQ + 8192, &maps.qp, 64, wr, hv, bar);
-        tma_load_3d(st + C::kOffK, &maps.k, 0, hq, t0, bar);
-        tma_load_3d(st + C::kOffK + 8192, &maps.k, 64, hq, t0, bar);
-        tma_load_3d(st + C::kOffU, &maps.u, v0, wr, hv, bar);
-        tma_load_3d(st + C::kOffO, &maps.oi, v0, wr, hv, bar);
-        tma_load_3d(st + C::kOffG, &maps.g4, 0, wr, hv, bar);
-    };
     if (tid == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, C::kMath / 32);
+            mbar_init(empty + s, kMathWarps);
         }
         *abort_flag = 0;
         mbar_fence_init();
     }
     __syncthreads();
-    if (warp == C::kMath / 32) {
+    if (warp == kMathWarps) {
         // Producer: refill stage c % 3 with chunk c once the math warps released chunk c - 3.
         if (lane == 0) {
             tma_prefetch_desc(&maps.w);
             tma_prefetch_desc(&maps.qp);
             tma_prefetch_desc(&maps.k);
-            tma_prefetch_desc(&maps.oi);
             tma_prefetch_desc(&maps.u);
+            tma_prefetch_desc(&maps.oi);
             tma_prefetch_desc(&maps.g4);
             for (int c = 0; c < nchunks; ++c) {
                 if (c >= C::kStages &&
                     !mbar_wait(empty + (c % C::kStages), (uint32_t)((c / C::kStages - 1) & 1), p.status,
                                kErrScanTmaTimeout))
                     break;  // the math warps stopped; they also stop waiting for more chunks
-                issue(c);
+                unsigned char* st = sm + (c % C::kStages) * C::kStage;
+                uint64_t* bar = full + (c % C::kStages);
+                const int wr = (slot0 + c) * kChunk, t0 = bos + c * kChunk;
+                mbar_arrive_expect_tx(bar, C::kTxBytes);
+                tma_load_3d(st + C::kOffW, &maps.w, 0, wr, hv, bar);
+                tma_load_3d(st + C::kOffW + 8192, &maps.w, 64, wr, hv, bar);
+                tma_load_3d(st + C::kOffQ, &maps.qp, 0, wr, hv, bar);
+                tma_load_3d(st + C::kOffQ + 8192, &maps.qp, 64, wr, hv, bar);
+                tma_load_3d(st + C::kOffK, &maps.k, 0, hq, t0, bar);
+                tma_load_3d(st + C::kOffK + 8192, &maps.k, 64, hq, t0, bar);
+                tma_load_3d(st + C::kOffU, &maps.u, v0, wr, hv, bar);
+                tma_load_3d(st + C::kOffO, &maps.oi, v0, wr, hv, bar);
+                tma_load_3d(st + C::kOffG, &maps.g4, 0, wr, hv, bar);
             }
         }
         return;
     }
 
-    // state slice h[kdim][v] as mma C fragments: rows 32*warp + 16*mt + gq (+8), cols 8*nt + 2*tq (+1)
-    float h[2][NT8][4];
+    // Math warp mw owns state rows (K dimension) 16 mw .. 16 mw + 15 as mma C fragments:
+    // h[nt][e] = h[16 mw + gq + 8 (e >> 1)][8 nt + 2 tq + (e & 1)].
+    const int mw = warp;
+    float h[NT8][4];
     {
         const float* st_in = p.state ? p.state + ((size_t)n * kHV + hv) * kD * kD : nullptr;
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
+        for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
-            for (int nt = 0; nt < NT8; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int row = 32 * warp + 16 * mt + gq + 8 * (e >> 1);
-                    const int col = 8 * nt + 2 * tq + (e & 1);
-                    h[mt][nt][e] = st_in ? st_in[(size_t)(v0 + col) * kD + row] : 0.f;
-                }
+            for (int e = 0; e < 4; ++e) {
+                const int row = 16 * mw + gq + 8 * (e >> 1);
+                const int col = 8 * nt + 2 * tq + (e & 1);
+                h[nt][e] = st_in ? st_in[(size_t)(v0 + col) * kD + row] : 0.f;
+            }
     }
     auto write_hb = [&]() {
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
+        for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
-            for (int nt = 0; nt < NT8; ++nt)
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const int row = 32 * warp + 16 * mt + gq + 8 * half;
-                    *reinterpret_cast<uint32_t*>(Hb + row * HS + 8 * nt + 2 * tq) =
-                        pack_bf16x2(h[mt][nt][2 * half], h[mt][nt][2 * half + 1]);
-                }
+            for (int half = 0; half < 2; ++half) {
+                const int row = 16 * mw + gq + 8 * half;
+                *reinterpret_cast<uint32_t*>(Hb + row * HS + 8 * nt + 2 * tq) =
+                    pack_bf16x2(h[nt][2 * half], h[nt][2 * half + 1]);
+            }
     };
     write_hb();
     named_bar_sync(1, C::kMath);
 
-    const bool dbg = blockIdx.x == 0 && blockIdx.y == 0;
+    const bool dbg = blockIdx.x == 0 && blockIdx.y == 0 && mw == 0;
     long long tp = clock64();
     (void)dbg;
+    const int prow0 = 16 * (mw & 3);  // rows of w h (warps 0-3) or Q' h (warps 4-7)
+    const bool out_warp = mw >= 4;
     int c = 0;
     for (; c < nchunks; ++c) {
         if (!mbar_wait(full + (c % C::kStages), (uint32_t)((c / C::kStages) & 1), p.status, kErrScanTmaTimeout))
             *abort_flag = 1;  // checked by every math thread after the next barrier
         GDN_PH_ACC(dbg, 20, tp);
-
         const unsigned char* st = sm + (c % C::kStages) * C::kStage;
-        const unsigned char* Ws = st + C::kOffW;
-        const unsigned char* Qs = st + C::kOffQ;
         const unsigned char* Ks = st + C::kOffK;
         const float* Us = reinterpret_cast<const float*>(st + C::kOffU);
         const uint16_t* Os = reinterpret_cast<const uint16_t*>(st + C::kOffO);
@@ -200,48 +201,57 @@ __global__ void __launch_bounds__(160, 1)
         const int L = min(kChunk, eos - t0);
         const float GL = G4[(L - 1) * 4];
 
-        // (1) P1 = W h, P2 = Q h   (rows 16*warp .. +15)
-        float p1[NT8][4], p2[NT8][4];
+        // (1) P = W h (warps 0-3) or Q' h (warps 4-7), rows prow0 .. +15; even / odd k-steps
+        //     accumulate separately to halve the dependent-MMA chain.
+        {
+            const unsigned char* At = st + (out_warp ? C::kOffQ : C::kOffW);
+            float pa[NT8][4], pb[NT8][4];
 #pragma unroll
-        for (int nt = 0; nt < NT8; ++nt)
+            for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) p1[nt][e] = p2[nt][e] = 0.f;
+                for (int e = 0; e < 4; ++e) pa[nt][e] = pb[nt][e] = 0.f;
 #pragma unroll
-        for (int k0 = 0; k0 < 128; k0 += 16) {
-            uint32_t aw[4], aq[4], b[NT8][2];
-            const int ar = 16 * warp + (lane & 15), ac = k0 + ((lane >> 4) << 3);
-            ldsm_x4(aw[0], aw[1], aw[2], aw[3], Ws + sw128_off(ar, ac, 8192));
-            ldsm_x4(aq[0], aq[1], aq[2], aq[3], Qs + sw128_off(ar, ac, 8192));
-            load_b_frags<NT8, HS>(b, Hb, k0, lane);
+            for (int k0 = 0; k0 < 128; k0 += 16) {
+                uint32_t a[4], b[NT8][2];
+                ldsm_x4(a[0], a[1], a[2], a[3], At + sw128_off(prow0 + (lane & 15), k0 + ((lane >> 4) << 3), 8192));
+                load_b_frags<NT8, HS>(b, Hb, k0, lane);
 #pragma unroll
-            for (int nt = 0; nt < NT8; ++nt) {
-                mma_bf16(p1[nt], aw, b[nt][0], b[nt][1]);
-                mma_bf16(p2[nt], aq, b[nt][0], b[nt][1]);
+                for (int nt = 0; nt < NT8; ++nt) {
+                    if ((k0 >> 4) & 1)
+                        mma_bf16(pb[nt], a, b[nt][0], b[nt][1]);
+                    else
+                        mma_bf16(pa[nt], a, b[nt][0], b[nt][1]);
+                }
             }
-        }
-        GDN_PH_ACC(dbg, 21, tp);
-        // (2) vn = u - P1 -> decayed vn (hi + lo) for the state update; o = scale (P2 + oi) -> out
+            GDN_PH_ACC(dbg, 21, tp);
+            // (2) warps 0-3: vn = u - W h -> decayed vn (bf16 hi + lo) for the state update;
+            //     warps 4-7: o = scale (Q' h + oi) -> out
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            const int row = 16 * warp + gq + 8 * half;
-            const float ed = __expf(GL - G4[row * 4]);  // <= 1; padded rows have vn = 0
-            uint16_t* dst = p.out + ((size_t)(t0 + row) * kHV + hv) * kD + v0;
+            for (int half = 0; half < 2; ++half) {
+                const int row = prow0 + gq + 8 * half;
+                if (!out_warp) {
+                    const float ed = __expf(GL - G4[row * 4]);  // <= 1; padded rows have vn = 0
 #pragma unroll
-            for (int nt = 0; nt < NT8; ++nt) {
-                const int col = 8 * nt + 2 * tq;
-                const float2 uu = *reinterpret_cast<const float2*>(Us + row * BV + col);
-                const float vn0 = uu.x - p1[nt][2 * half];
-                const float vn1 = uu.y - p1[nt][2 * half + 1];
-                const float d0 = vn0 * ed, d1 = vn1 * ed;
-                const uint32_t hi = pack_bf16x2(d0, d1);
-                *reinterpret_cast<uint32_t*>(VNh + row * HS + col) = hi;
-                *reinterpret_cast<uint32_t*>(VNl + row * HS + col) =
-                    pack_bf16x2(d0 - __uint_as_float(hi << 16), d1 - __uint_as_float(hi & 0xffff0000u));
-                if (row < L) {
-                    const uint32_t oo = *reinterpret_cast<const uint32_t*>(Os + row * BV + col);
-                    *reinterpret_cast<uint32_t*>(dst + col) =
-                        pack_bf16x2(p.scale * (p2[nt][2 * half] + __uint_as_float(oo << 16)),
-                                    p.scale * (p2[nt][2 * half + 1] + __uint_as_float(oo & 0xffff0000u)));
+                    for (int nt = 0; nt < NT8; ++nt) {
+                        const int col = 8 * nt + 2 * tq;
+                        const float2 uu = *reinterpret_cast<const float2*>(Us + row * BV + col);
+                        const float d0 = (uu.x - (pa[nt][2 * half] + pb[nt][2 * half])) * ed;
+                        const float d1 = (uu.y - (pa[nt][2 * half + 1] + pb[nt][2 * half + 1])) * ed;
+                        const uint32_t hi = pack_bf16x2(d0, d1);
+                        *reinterpret_cast<uint32_t*>(VNh + row * HS + col) = hi;
+                        *reinterpret_cast<uint32_t*>(VNl + row * HS + col) =
+                            pack_bf16x2(d0 - __uint_as_float(hi << 16), d1 - __uint_as_float(hi & 0xffff0000u));
+                    }
+                } else if (row < L) {
+                    uint16_t* dst = p.out + ((size_t)(t0 + row) * kHV + hv) * kD + v0;
+#pragma unroll
+                    for (int nt = 0; nt < NT8; ++nt) {
+                        const int col = 8 * nt + 2 * tq;
+                        const uint32_t oo = *reinterpret_cast<const uint32_t*>(Os + row * BV + col);
+                        *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16x2(
+                            p.scale * (pa[nt][2 * half] + pb[nt][2 * half] + __uint_as_float(oo << 16)),
+                            p.scale * (pa[nt][2 * half + 1] + pb[nt][2 * half + 1] + __uint_as_float(oo & 0xffff0000u)));
+                    }
                 }
             }
         }
@@ -250,33 +260,32 @@ __global__ void __launch_bounds__(160, 1)
         GDN_PH_ACC(dbg, 23, tp);
         if (*abort_flag) break;  // written only before this barrier: every math thread sees the same value
 
-        // (3b) h = e^{GL} h + K^T (vn_hi + vn_lo)   (rows 32*warp .. +31 of the K dimension)
+        // (3) h = e^{GL} h + K^T (vn_hi + vn_lo) for state rows 16 mw .. +15 (hi and lo parts
+        //     accumulate separately, chain of 4 MMAs each)
         {
-            const float eL = __expf(GL);
+            float dh[NT8][4], dl[NT8][4];
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+            for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
-                for (int nt = 0; nt < NT8; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) h[mt][nt][e] *= eL;
+                for (int e = 0; e < 4; ++e) dh[nt][e] = dl[nt][e] = 0.f;
 #pragma unroll
             for (int k0 = 0; k0 < 64; k0 += 16) {
-                uint32_t a[2][4], bh[NT8][2], bl[NT8][2];
-#pragma unroll
-                for (int mt = 0; mt < 2; ++mt)
-                    ldsm_x4_t(a[mt][0], a[mt][1], a[mt][2], a[mt][3],
-                              Ks + sw128_off(k0 + (lane & 7) + ((lane >> 4) << 3),
-                                             32 * warp + 16 * mt + (((lane >> 3) & 1) << 3), 8192));
+                uint32_t a[4], bh[NT8][2], bl[NT8][2];
+                ldsm_x4_t(a[0], a[1], a[2], a[3],
+                          Ks + sw128_off(k0 + (lane & 7) + ((lane >> 4) << 3), 16 * mw + (((lane >> 3) & 1) << 3), 8192));
                 load_b_frags<NT8, HS>(bh, VNh, k0, lane);
                 load_b_frags<NT8, HS>(bl, VNl, k0, lane);
 #pragma unroll
-                for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                    for (int nt = 0; nt < NT8; ++nt) {
-                        mma_bf16(h[mt][nt], a[mt], bh[nt][0], bh[nt][1]);
-                        mma_bf16(h[mt][nt], a[mt], bl[nt][0], bl[nt][1]);
-                    }
+                for (int nt = 0; nt < NT8; ++nt) {
+                    mma_bf16(dh[nt], a, bh[nt][0], bh[nt][1]);
+                    mma_bf16(dl[nt], a, bl[nt][0], bl[nt][1]);
+                }
             }
+            const float eL = __expf(GL);
+#pragma unroll
+            for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) h[nt][e] = fmaf(eL, h[nt][e], dh[nt][e] + dl[nt][e]);
         }
         GDN_PH_ACC(dbg, 24, tp);
         __syncwarp();
@@ -295,15 +304,13 @@ __global__ void __launch_bounds__(160, 1)
 
     // final state (k-last): new_state[n][hv][v0 + col][row]
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < NT8; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = 32 * warp + 16 * mt + gq + 8 * (e >> 1);
-                const int col = 8 * nt + 2 * tq + (e & 1);
-                st_out[(size_t)(v0 + col) * kD + row] = h[mt][nt][e];
-            }
+        for (int e = 0; e < 4; ++e) {
+            const int row = 16 * mw + gq + 8 * (e >> 1);
+            const int col = 8 * nt + 2 * tq + (e & 1);
+            st_out[(size_t)(v0 + col) * kD + row] = h[nt][e];
+        }
 }
 
 template <int BV>
