@@ -11,6 +11,7 @@
 #include "common.cuh"
 
 #include "kernels.cuh"
+#include "prefill_kernels.cuh"
 
 namespace {
 
@@ -116,6 +117,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.N = N;
     p.T = T;
     p.S = lay.S;
+    p.small_n = N <= gdn::kSmallN ? 1 : 0;
     p.scale = scale;
     p.out = static_cast<uint16_t*>(out);
     p.new_state = new_state;

@@ -35,6 +35,8 @@ struct PrefillArgs {
     int cu64;
     int N, T;
     int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
+    int small_n;           // 1: N is small enough for each CTA to derive its chunk slots itself
+                           //    (no chunk-table launch); 0: read chunk_base / chunk_seq
     float scale;
     uint16_t* out;         // [T, 8, 128]
     float* new_state;      // [N, 8, 128, 128]

@@ -11,10 +11,12 @@
 namespace gdn {
 
 int prefill_scan_bv(int N) {
-    // (128 / BV) * N * 8 CTAs: small batches split the state columns finer to cover the SMs.
-    if (N * kHV * (kD / 32) >= 296) return 32;
-    if (N * kHV * (kD / 16) >= 148) return 16;
-    return 8;
+    // (128 / BV) * N * 8 CTAs, one per SM (the 3-stage TMA ring fills shared memory).  Finer
+    // slices only pay while they fit in one wave of 148 SMs; past that, wider slices amortise
+    // the per-chunk W / Q' / K tile traffic over more state columns (measured on B200).
+    if (N * kHV * (kD / 8) <= 148) return 8;
+    if (N * kHV * (kD / 16) <= 148) return 16;
+    return 32;
 }
 
 // ---- chunk table ---------------------------------------------------------------------------
@@ -124,7 +126,7 @@ bool build_prefill_maps(const PrefillArgs& p, int bv, PrefillMaps* m) {
 
 int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream) {
     if (p.N <= 0) return 0;
-    gdn_prefill_table_kernel<<<1, 1024, 0, stream>>>(p);
+    if (!p.small_n) gdn_prefill_table_kernel<<<1, 1024, 0, stream>>>(p);
     if (p.T > 0) {
         PrefillMaps maps;
         if (!build_prefill_maps(p, bv, &maps)) return -3;

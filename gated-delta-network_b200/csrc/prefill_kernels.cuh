@@ -40,6 +40,35 @@ __device__ __forceinline__ void seq_bounds(const void* cu, int cu64, int n, int 
     e = (int)b;
 }
 
+// Up to this many sequences the prep and scan kernels derive their chunk slots from
+// cu_seqlens directly (one warp, one load per lane); above it a one-CTA table kernel computes
+// chunk_base / chunk_seq once per call.
+constexpr int kSmallN = 32;
+
+__device__ __forceinline__ int seq_nchunks(const PrefillArgs& p, int i) {
+    int s, e;
+    seq_bounds(p.cu, p.cu64, i, p.T, s, e);
+    return (e - s + kChunk - 1) / kChunk;
+}
+
+// Warp-wide, N <= 32: first slot of sequence `n` (chunk_base[n]) and the sequence owning
+// `slot` (-1 if none, or if slot < 0).  Every lane returns the same values.
+__device__ __forceinline__ void warp_chunk_lookup(const PrefillArgs& p, int n, int slot, int* base_out, int* seq_out) {
+    const int lane = threadIdx.x & 31;
+    const int nc = lane < p.N ? seq_nchunks(p, lane) : 0;
+    int x = nc;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    const int excl = x - nc;
+    const int total = __shfl_sync(0xffffffffu, x, 31);
+    *base_out = n >= p.N ? total : __shfl_sync(0xffffffffu, excl, n & 31);
+    const unsigned owner = __ballot_sync(0xffffffffu, lane < p.N && nc > 0 && slot >= excl && slot < excl + nc);
+    *seq_out = owner ? __ffs(owner) - 1 : -1;
+}
+
 bool build_prefill_maps(const PrefillArgs& p, int bv, PrefillMaps* m);
 int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream);

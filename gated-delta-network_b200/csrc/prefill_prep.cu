@@ -90,11 +90,33 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;
     const int slot = blockIdx.x, hv = blockIdx.y, hq = hv / (kHV / kH);
-    const int seq = p.chunk_seq[slot];
-    if (seq < 0) return;  // unused slot (uniform across the CTA)
+    int seq, cbase;
+    if (p.small_n) {
+        // warp 0 finds the slot's sequence; the result is published through shared memory
+        __shared__ int s_lookup[2];
+        if (warp == 0) {
+            int base_dummy, sq;
+            warp_chunk_lookup(p, 0, slot, &base_dummy, &sq);
+            int cb = 0;
+            if (sq >= 0) warp_chunk_lookup(p, sq, -1, &cb, &base_dummy);
+            if (lane == 0) {
+                s_lookup[0] = sq;
+                s_lookup[1] = cb;
+                if (slot == 0 && hv == 0) atomicExch(p.status, 0);  // no table kernel ran this call
+            }
+        }
+        __syncthreads();
+        seq = s_lookup[0];
+        cbase = s_lookup[1];
+        if (seq < 0) return;  // unused slot (uniform across the CTA)
+    } else {
+        seq = p.chunk_seq[slot];
+        if (seq < 0) return;
+        cbase = p.chunk_base[seq];
+    }
     int s0, e0;
     seq_bounds(p.cu, p.cu64, seq, p.T, s0, e0);
-    const int bos = s0 + (slot - p.chunk_base[seq]) * kChunk;
+    const int bos = s0 + (slot - cbase) * kChunk;
     const int L = min(kChunk, e0 - bos);
     const size_t row0 = (size_t)hv * p.S * kChunk + (size_t)slot * kChunk;  // workspace row of token bos
     long long tp = clock64();

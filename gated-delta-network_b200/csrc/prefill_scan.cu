@@ -111,7 +111,13 @@ __global__ void __launch_bounds__(288, 1)
         return;
     }
     const int nchunks = (len + kChunk - 1) / kChunk;
-    const int slot0 = p.chunk_base[n];
+    int slot0;
+    if (p.small_n) {
+        int dummy;
+        warp_chunk_lookup(p, n, -1, &slot0, &dummy);  // every warp computes the same value
+    } else {
+        slot0 = p.chunk_base[n];
+    }
 
     if (tid == 0) {
         for (int s = 0; s < C::kStages; ++s) {

@@ -188,3 +188,22 @@ def test_prefill_8k_single_sequence():
 def test_prefill_packed_8x1024():
     inp = gi.prefill_inputs([1024] * 8, seed=1, with_state=True)
     _run_and_check(inp)
+
+
+def test_prefill_many_sequences_chunk_table_path():
+    """More than 32 sequences: slots come from the one-CTA chunk-table kernel instead of a
+    per-warp lookup; includes zero-length and single-token sequences."""
+    rng = np.random.default_rng(31)
+    lens = rng.integers(0, 90, 300).tolist()
+    lens[5] = 0
+    lens[7] = 1
+    inp = gi.prefill_inputs(lens, seed=31)
+    _run_and_check(inp)
+
+
+def test_prefill_more_sequences_than_one_table_tile():
+    """1100 short sequences: the chunk-table kernel's prefix sum spans two 1024-thread tiles."""
+    rng = np.random.default_rng(32)
+    lens = rng.integers(0, 4, 1100).tolist()
+    inp = gi.prefill_inputs(lens, seed=32)
+    _run_and_check(inp)
