@@ -9,6 +9,8 @@ Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed
     (8 x 32 MiB = 256 MiB > the 126 MB L2, so every launch streams its state from HBM).
   * prefill_8k: one 8192-token sequence (cu_seqlens = [0, 8192], initial state N(0, 0.02)),
     tokens/s; L2 flushed (256 MiB write) before every timed step, per-step CUDA events.
+  * prefill_configs: one 1024-token sequence, 16 log-uniform varlen sequences (total <= 32768)
+    and 8 packed 1024-token sequences, timed the same way.
   * e2e: the same two metrics through the public API (gdn.decode.kernel / gdn.prefill.kernel)
     with pinned host buffers: every step copies its inputs host->device and its results back.
   * cpu_baseline: the CPU oracle (a C restatement of the reference's sequential PyTorch
@@ -49,7 +51,7 @@ N_STATE_BUFS = 8
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum), or None.
 # Source: the ncu summaries under profiles/ (decode B=64 launch; prefill kernels at T=8192).
 # decode: 33.83 MB read; the 33.55 MB of state writes are still dirty in L2 when ncu's replayed launch ends.
-NCU_TRAFFIC = {"decode": 33831424, "prefill_scan": 86445568}
+NCU_TRAFFIC = {"decode": 33831424, "prefill_scan": 103006976}
 
 
 def env_int(name, default):
@@ -334,6 +336,43 @@ def main():
     pre_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / len(evs)
     pre_ms = max_over_ranks(pre_ms)
 
+    # ---------------- other prefill configurations (reported alongside) ----------------
+    def time_prefill(lens, with_state, steps=10):
+        Tn, Nn = int(sum(lens)), len(lens)
+        xq, xk = l2n(randn((Tn, H, D))), l2n(randn((Tn, H, D)))
+        xv = randn((Tn, HV, D), dtype=torch.bfloat16)
+        xa, xb = randn((Tn, HV), dtype=torch.bfloat16), randn((Tn, HV), dtype=torch.bfloat16)
+        xh = randn((Nn, HV, D, D), 0.02) if with_state else None
+        xcu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device=dev)
+        xo = torch.empty((Tn, HV, D), dtype=torch.bfloat16, device=dev)
+        xs = torch.empty((Nn, HV, D, D), dtype=torch.float32, device=dev)
+        xws = torch.empty(gdn.prefill.workspace_bytes(Nn, Tn), dtype=torch.uint8, device=dev)
+
+        def step():
+            pmod._launch(xq, xk, xv, xh, A_log, xa, dt_bias, xb, xcu, scale, xo, xs, workspace=xws)
+
+        for _ in range(3):
+            step()
+        barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            flush.fill_(1)
+            e0.record()
+            step()
+            e1.record()
+        barrier()
+        ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps)
+        return {"tokens_per_s": round(world * Tn / (ms * 1e-3), 1), "ms_per_step": round(ms, 5), "tokens": Tn,
+                "sequences": Nn}
+
+    from tests.golden.inputs import varlen_lengths  # seeded log-uniform lengths (numpy only)
+
+    prefill_more = {
+        "1x1024 (config 2, zero initial state)": time_prefill([1024], False),
+        "16 varlen, log-uniform [6, 8192] (config 3)": time_prefill(varlen_lengths(), True),
+        "8x1024 packed": time_prefill([1024] * 8, True),
+    }
+
     # ---------------- e2e through the public API with pinned host buffers ----------------
     e2e = None
     pre_e2e = None
@@ -405,7 +444,7 @@ def main():
     cpu = None
     if not args.no_cpu_baseline:
         cpu = cpu_decode_baseline(budget_s=args.cpu_budget)
-        cpu_pre = cpu_prefill_baseline(1024)
+        cpu_pre = cpu_prefill_baseline(8192)
     dec_us = dec_ms * 1e3
     value = world * DECODE_STATE_BYTES / (dec_ms * 1e-3) / 1e9
     achieved = DECODE_ALG_BYTES / (dec_ms * 1e-3) / 1e9
@@ -442,6 +481,7 @@ def main():
                          "traffic": NCU_TRAFFIC["prefill_scan"], "peak_source": peak_src},
             "e2e": pre_e2e,
         },
+        "prefill_configs": prefill_more,
         "e2e": e2e,
         "gpu_launches": steps,
         "clocks": clock_summary,
