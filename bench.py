@@ -126,9 +126,19 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
+def host_threads():
+    """Cores this process may run on (torchrun sets OMP_NUM_THREADS=1, which must not shrink the baseline)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_decode_baseline(budget_s=10.0, threads=0):
     """CPU oracle on decode B=64 (same inputs as the headline), repeated for ~budget_s."""
     from oracle import oracle
+
+    threads = threads or host_threads()
     from tests.golden import inputs as gi
 
     inp = gi.decode_inputs(DECODE_B, seed=0)
@@ -152,6 +162,8 @@ def cpu_decode_baseline(budget_s=10.0, threads=0):
 def cpu_prefill_baseline(tokens=1024, threads=0):
     """CPU oracle on the first `tokens` tokens of one sequence: tokens/s (the oracle is linear in T)."""
     from oracle import oracle
+
+    threads = threads or host_threads()
     from tests.golden import inputs as gi
 
     inp = gi.prefill_inputs([tokens], seed=0, with_state=True)
@@ -169,7 +181,7 @@ def run_reference_arm(args, rank, world):
         return
     from oracle import oracle
 
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     for _ in range(args.warmup):
         cpu_decode_baseline(budget_s=0.0, threads=threads)
     times = []
