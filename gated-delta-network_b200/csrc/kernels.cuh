@@ -35,6 +35,7 @@ struct PrefillArgs {
     int cu64;
     int N, T;
     int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
+    int test_withhold;     // GDN_FLAG_TEST_WITHHOLD_CHUNK: the scan skips chunk 1's copies
     int small_n;           // 1: N is small enough for each CTA to derive its chunk slots itself
                            //    (no chunk-table launch); 0: read chunk_base / chunk_seq
     float scale;

@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(288, 1)
                     !mbar_wait(empty + (c % C::kStages), (uint32_t)((c / C::kStages - 1) & 1), p.status,
                                kErrScanTmaTimeout))
                     break;  // the math warps stopped; they also stop waiting for more chunks
+                if (p.test_withhold && c == 1) continue;  // test hook: this chunk's copies never arrive
                 unsigned char* st = sm + (c % C::kStages) * C::kStage;
                 uint64_t* bar = full + (c % C::kStages);
                 const int wr = (slot0 + c) * kChunk, t0 = bos + c * kChunk;

@@ -14,7 +14,8 @@
 
 namespace gdn {
 
-// Error codes written to the workspace status word when a bounded wait gives up.
+// Error codes written to the workspace status word when a bounded wait gives up
+// (GDN_DEVSTATUS_* in include/gdn_b200.h).
 constexpr int kErrScanTmaTimeout = 1;
 constexpr int kErrPrepTmaTimeout = 2;
 constexpr int kErrPrepMmaTimeout = 3;

@@ -75,6 +75,13 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     _lib.check("gdn_prefill_fwd", rc)
 
 
+def read_status(workspace: torch.Tensor) -> int:
+    """Device status word of the last call that used `workspace` (0 = ok; 1..3 = a bounded
+    device-side wait gave up, see GDN_DEVSTATUS_* in include/gdn_b200.h).  Reads device memory,
+    so it synchronises with the current stream: a debugging aid, not part of the hot path."""
+    return int(workspace[:4].view(torch.int32).item())
+
+
 @torch.no_grad()
 def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
     """Varlen prefill.  Returns ``(output [T,8,128] bf16, new_state [N,8,128,128] fp32)``.

@@ -37,8 +37,21 @@ enum gdn_status {
     GDN_ERR_DEVICE = 7     /* current device is not sm_100 (B200)                 */
 };
 
-/* Flags (bitwise OR) accepted by the entry points. */
+/* Flags (bitwise OR) accepted by the entry points.
+ * Bits 8-15 (value << 8) force a kernel variant for tuning: the decode CTA tiling (variant + 1)
+ * or the prefill scan's state-column slice width (8, 16 or 32); 0 lets the library choose. */
 #define GDN_FLAG_NONE 0u
+/* Failure-detection test hook for gdn_prefill_fwd: the scan kernel withholds the TMA copies of
+ * each sequence's second chunk, so its bounded wait expires (after about 2 s), the call records
+ * GDN_DEVSTATUS_SCAN_TMA_TIMEOUT in the workspace status word and returns without hanging.
+ * Outputs of such a call are invalid.  Never set in production. */
+#define GDN_FLAG_TEST_WITHHOLD_CHUNK 0x1u
+
+/* Device-side status codes written to the first int of the prefill workspace. */
+#define GDN_DEVSTATUS_OK 0
+#define GDN_DEVSTATUS_SCAN_TMA_TIMEOUT 1
+#define GDN_DEVSTATUS_PREP_TMA_TIMEOUT 2
+#define GDN_DEVSTATUS_PREP_MMA_TIMEOUT 3
 
 /* Fixed shape family (the reference asserts exactly these:
  * reference/gdn_decode_ref.py:32-36, reference/gdn_prefill_ref.py:33-36). */

@@ -207,3 +207,26 @@ def test_prefill_more_sequences_than_one_table_tile():
     lens = rng.integers(0, 4, 1100).tolist()
     inp = gi.prefill_inputs(lens, seed=32)
     _run_and_check(inp)
+
+
+@pytest.mark.timeout(120)
+def test_prefill_bounded_wait_reports_and_recovers():
+    """Failure detection without a GPU fault: with the test hook the scan's producer withholds a
+    chunk's TMA copies, the math warps' bounded mbarrier wait expires, the kernel records status 1
+    in the workspace and returns; the context stays usable and the next call is correct."""
+    from gdn import prefill as pmod
+
+    inp = gi.prefill_inputs([200], seed=33)
+    args = util.prefill_args(inp)
+    out = torch.empty(200, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(1, 8, 128, 128, dtype=torch.float32, device="cuda")
+    ws = torch.empty(gdn.prefill.workspace_bytes(1, 200), dtype=torch.uint8, device="cuda")
+    pmod._launch(*args, out, ns, workspace=ws, flags=1)  # GDN_FLAG_TEST_WITHHOLD_CHUNK
+    torch.cuda.synchronize()
+    assert gdn.prefill.read_status(ws) == 1  # GDN_DEVSTATUS_SCAN_TMA_TIMEOUT
+    pmod._launch(*args, out, ns, workspace=ws)
+    torch.cuda.synchronize()
+    assert gdn.prefill.read_status(ws) == 0
+    ro, rs = _oracle(inp)
+    util.check_out(util.bits(out), ro)
+    util.check_state(ns.cpu().numpy(), rs)
