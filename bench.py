@@ -10,7 +10,8 @@ Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed
   * prefill_8k: one 8192-token sequence (cu_seqlens = [0, 8192], initial state N(0, 0.02)),
     tokens/s; L2 flushed (256 MiB write) before every timed step, per-step CUDA events.
   * prefill_configs: one 1024-token sequence, 16 log-uniform varlen sequences (total <= 32768)
-    and 8 packed 1024-token sequences, timed the same way.
+    and 8 packed 1024-token sequences per GPU, timed the same way; plus 64 x 4096 tokens split by
+    sequence over the ranks (strong scaling; whole-job tokens/s over the slowest rank).
   * e2e: the same two metrics through the public API (gdn.decode.kernel / gdn.prefill.kernel)
     with pinned host buffers: every step copies its inputs host->device and its results back.
   * cpu_baseline: the CPU oracle (a C restatement of the reference's sequential PyTorch
@@ -379,10 +380,20 @@ def main():
 
     from tests.golden.inputs import varlen_lengths  # seeded log-uniform lengths (numpy only)
 
+    from gdn.shard import seq_shard
+
+    # config 4: 64 x 4096 tokens partitioned by sequence over the ranks (strong scaling, no collective)
+    c4_cu = [4096 * i for i in range(65)]
+    _, _, c4_t0, c4_t1, c4_local = seq_shard(c4_cu, world, rank)
+    c4 = time_prefill([c4_local[i + 1] - c4_local[i] for i in range(len(c4_local) - 1)], True, steps=3)
+    c4["tokens_per_s"] = round(64 * 4096 / (c4["ms_per_step"] * 1e-3), 1)  # whole job over max-rank time
+    c4["scaling"] = "strong: 64 sequences x 4096 tokens split over the ranks"
+
     prefill_more = {
         "1x1024 (config 2, zero initial state)": time_prefill([1024], False),
         "16 varlen, log-uniform [6, 8192] (config 3)": time_prefill(varlen_lengths(), True),
         "8x1024 packed": time_prefill([1024] * 8, True),
+        "64x4096 partitioned (config 4)": c4,
     }
 
     # ---------------- e2e through the public API with pinned host buffers ----------------
