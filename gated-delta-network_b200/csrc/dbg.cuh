@@ -16,7 +16,20 @@ static __device__ long long gdn_dbg_clk[64];
             prev = now_;                          \
         }                                         \
     } while (0)
+// Same, measured by thread `who` instead of thread 0.
+#define GDN_PH_ACC_T(cond, who, slot, prev)       \
+    do {                                          \
+        if ((cond) && threadIdx.x == (who)) {     \
+            const long long now_ = clock64();     \
+            atomicAdd((unsigned long long*)&gdn_dbg_clk[slot], (unsigned long long)(now_ - (prev))); \
+            prev = now_;                          \
+        }                                         \
+    } while (0)
 #else
+#define GDN_PH_ACC_T(cond, who, slot, prev) \
+    do {                                   \
+        (void)(prev);                      \
+    } while (0)
 #define GDN_DBG_READER(name)
 #define GDN_PH_ACC(cond, slot, prev) \
     do {                             \

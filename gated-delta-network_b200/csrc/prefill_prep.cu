@@ -50,7 +50,8 @@ constexpr uint32_t kOffG = kOffY + 4 * 16 * 17 * 4;
 constexpr uint32_t kOffB = kOffG + 64 * 4;
 constexpr uint32_t kOffE = kOffB + 64 * 4;
 constexpr uint32_t kOffGf = kOffE + 64 * 4;    // [64] f32 final cumulative log decay
-constexpr uint32_t kOffBar = kOffGf + 64 * 4;  // 2 mbarriers
+constexpr uint32_t kOffBt = kOffGf + 64 * 4;   // [64] f32 exp(G_r(j) - G_j), r(j) = last token of j's 16-block
+constexpr uint32_t kOffBar = kOffBt + 64 * 4;  // 2 mbarriers
 constexpr uint32_t kOffSlot = kOffBar + 16;
 static_assert(kOffSlot + 16 <= 8192, "misc block");
 constexpr uint32_t kTmemCols = 256;
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     float* Bs = reinterpret_cast<float*>(misc + kOffB);
     float* Es = reinterpret_cast<float*>(misc + kOffE);
     float* Gf = reinterpret_cast<float*>(misc + kOffGf);
+    float* Bt = reinterpret_cast<float*>(misc + kOffBt);
     uint64_t* bar_load = reinterpret_cast<uint64_t*>(misc + kOffBar);
     uint64_t* bar_mma = bar_load + 1;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(misc + kOffSlot);
@@ -166,8 +168,10 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     // Padded tokens (t >= L) carry g = 0, so their cumulative G repeats G_{L-1}.
     if (tid < 64) {
         const float x = Gs[tid] + (tid >= 32 ? Gs[31] : 0.f);
+        const float xr = __shfl_sync(0xffffffffu, x, (lane & 16) | 15);  // G at the end of this 16-block
         Gf[tid] = x;
         Es[tid] = __expf(x);
+        Bt[tid] = __expf(fminf(xr - x, 0.f));
     }
     bool ok = mbar_wait(bar_load, 0, p.status, kErrPrepTmaTimeout);
     ok = __syncthreads_and(ok);  // also publishes Gf / Es
@@ -194,11 +198,18 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     GDN_PH_ACC(dbg, 1, tp);
     // ---- 3. epilogue #1: thread r owns TMEM lane r (rows 0-63: K K^T, rows 64-127: Q K^T) -----
     {
-        const int r = tid, i = r & 63;
+        long long tq3 = clock64();
+        const int r = tid, i = r & 63, I = i >> 4;
         const bool qk = r >= 64;
         const float Gi = Gf[i], bi = Bs[i];
         const bool live = i < L;
-        auto decay = [&](int j) -> float { return __expf(Gi - Gf[j]); };  // only formed for j <= i
+        // Decay exp(G_i - G_j), j <= i.  Below row i's 16-token block it factors exactly as
+        // a_i(J) * Bt[j] with a_i(J) = exp(G_i - G_r(J)), Bt[j] = exp(G_r(J) - G_j), r(J) = last token
+        // of block J: both factors are <= 1, so nothing overflows and only the diagonal block needs
+        // per-element exponentials.
+        float aJ[3];
+#pragma unroll
+        for (int J = 0; J < 3; ++J) aJ[J] = __expf(fminf(Gi - Gf[16 * J + 15], 0.f));
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
             if (half == 1 && (warp & 1) == 0) {
@@ -218,35 +229,47 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
             }
             float d[32];
             tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 32 * half, d);
-            if (!qk) {
+            GDN_PH_ACC_T(dbg, 96, 10, tq3);
+            // v[c] = masked, decayed value of column 32*half + c (row scale beta_i for A rows)
+            float v[32];
 #pragma unroll
-                for (int j4 = 0; j4 < 8; ++j4) {
-                    float4 o;
-                    float* po = &o.x;
+            for (int Jh = 0; Jh < 2; ++Jh) {
+                const int J = 2 * half + Jh;
+                if (J < I) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int j = 32 * half + 4 * j4 + e;
-                        po[e] = (live && j < i) ? bi * decay(j) * d[4 * j4 + e] : 0.f;
+                    for (int c = 0; c < 16; ++c) v[16 * Jh + c] = aJ[J < 3 ? J : 2] * Bt[16 * J + c] * d[16 * Jh + c];
+                } else if (J == I) {
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const int j = 16 * J + c;
+                        const bool keep = qk ? (j <= i) : (j < i);
+                        v[16 * Jh + c] = __expf(fminf(Gi - Gf[j], 0.f)) * (keep ? d[16 * Jh + c] : 0.f);
                     }
-                    *reinterpret_cast<float4*>(Af + i * kFS + 32 * half + 4 * j4) = o;
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) v[16 * Jh + c] = 0.f;
                 }
+            }
+            if (!qk) {
+                const float sc = live ? bi : 0.f;
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4)
+                    *reinterpret_cast<float4*>(Af + i * kFS + 32 * half + 4 * j4) =
+                        make_float4(sc * v[4 * j4], sc * v[4 * j4 + 1], sc * v[4 * j4 + 2], sc * v[4 * j4 + 3]);
             } else {
+                const float sc = live ? 1.f : 0.f;
 #pragma unroll
                 for (int j8 = 0; j8 < 4; ++j8) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int j0 = 32 * half + 8 * j8 + 2 * e;
-                        const float x0 = (live && j0 <= i) ? decay(j0) * d[8 * j8 + 2 * e] : 0.f;
-                        const float x1 = (live && j0 + 1 <= i) ? decay(j0 + 1) * d[8 * j8 + 2 * e + 1] : 0.f;
-                        pk[e] = pack_bf16x2(x0, x1);
-                    }
-                    const uint4 q4 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    const uint4 q4 = make_uint4(pack_bf16x2(sc * v[8 * j8], sc * v[8 * j8 + 1]),
+                                                pack_bf16x2(sc * v[8 * j8 + 2], sc * v[8 * j8 + 3]),
+                                                pack_bf16x2(sc * v[8 * j8 + 4], sc * v[8 * j8 + 5]),
+                                                pack_bf16x2(sc * v[8 * j8 + 6], sc * v[8 * j8 + 7]));
                     const uint32_t ch = (uint32_t)(4 * half + j8);
                     *reinterpret_cast<uint4*>(sm + kOffAq + i * 128 + ((ch ^ (uint32_t)(i & 7)) << 4)) = q4;
                     *reinterpret_cast<uint4*>(sm + kOffAq + (64 + i) * 128 + ((ch ^ (uint32_t)(i & 7)) << 4)) = q4;
                 }
             }
+            GDN_PH_ACC_T(dbg, 96, 11, tq3);
         }
         if (tid < 64) *reinterpret_cast<float4*>(p.g4 + (row0 + tid) * 4) = make_float4(Gf[tid], Es[tid], Bs[tid], 0.f);
     }
@@ -492,7 +515,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     }
 
 cleanup:
-    if (tid == 0) tma_store_wait_all();  // shared memory must outlive the stores that read it
+    // Shared memory must outlive the bulk stores that read it; their global writes complete
+    // before the grid does, so the scan kernel (a later launch on the stream) sees them.
+    if (tid == 0) tma_store_wait_read();
     GDN_PH_ACC(dbg, 8, tp);
     tc_fence_before();
     __syncthreads();
