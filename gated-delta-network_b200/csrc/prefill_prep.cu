@@ -1,6 +1,6 @@
 // prefill_prep.cu -- chunk-parallel half of the chunked Gated DeltaNet prefill (sm_100a).
 //
-// One CTA per (64-token chunk slot, v-head), 128 threads, two CTAs per SM.  For the chunk's
+// One CTA per (64-token chunk slot, v-head), 256 threads, two CTAs per SM.  For the chunk's
 // tokens t = bos .. bos+L-1 of v-head hv (q/k head hv/2) it computes, following the chunked
 // WY form of solutions/gdn_prefill_qk4_v8_d128_k_last/solution/triton/fla_kernels.py
 // (cumsum + K K^T 858-905, solve_tril 197-314, recompute_w_u 334-383):
@@ -30,7 +30,7 @@ GDN_DBG_READER(gdn_debug_read_prep)
 
 namespace gdn {
 namespace prep2 {
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;  // 8 warps: warps w and w+4 share TMEM lane quarter w % 4
 constexpr int kFS = 68;  // fp32 row stride of A / T (rows stay 16-byte aligned)
 constexpr uint32_t kOffK0 = 0;        // K cols 0-63   (64 rows x 128 B, SW128)
 constexpr uint32_t kOffQ0 = 8192;     // Q cols 0-63   -> [K;Q] is one 128-row operand
@@ -91,6 +91,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;
+    // Row-per-thread epilogues: thread rr owns TMEM lane / row rr, the two warpgroups split the
+    // columns (ch_half 0 / 1).  Warp w reads TMEM lane quarter w % 4.
+    const int rr = tid & 127, ch_half = tid >> 7, wq = warp & 3;
     const int slot = blockIdx.x, hv = blockIdx.y, hq = hv / (kHV / kH);
     int seq, cbase;
     if (p.small_n) {
@@ -126,14 +129,12 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     (void)dbg;
 
     // ---- 1. barriers, TMA loads, TMEM, gates ------------------------------------------------
+    // Thread 0 issues the tile loads first thing; the other threads touch the barriers only
+    // after the block barrier below, by which time their initialisation is visible.
     if (tid == 0) {
         mbar_init(bar_load, 1);
         mbar_init(bar_mma, 1);
         mbar_fence_init();
-    }
-    for (int i = tid; i < 64 * kFS; i += kThreads) Tf[i] = 0.f;
-    __syncthreads();
-    if (tid == 0) {
         mbar_arrive_expect_tx(bar_load, 6 * 8192);
         tma_load_3d(sm + kOffK0, &maps.k, 0, hq, bos, bar_load);
         tma_load_3d(sm + kOffK1, &maps.k, 64, hq, bos, bar_load);
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         tma_load_3d(sm + kOffV0, &maps.v, 0, hv, bos, bar_load);
         tma_load_3d(sm + kOffV1, &maps.v, 64, hv, bos, bar_load);
     }
+    for (int i = tid; i < 64 * kFS; i += kThreads) Tf[i] = 0.f;
     if (warp == 0) tmem_alloc(tslot, kTmemCols);
     if (tid < 64) {
         const int t = tid;
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     // ---- 3. epilogue #1: thread r owns TMEM lane r (rows 0-63: K K^T, rows 64-127: Q K^T) -----
     {
         long long tq3 = clock64();
-        const int r = tid, i = r & 63, I = i >> 4;
+        const int r = rr, i = r & 63, I = i >> 4;
         const bool qk = r >= 64;
         const float Gi = Gf[i], bi = Bs[i];
         const bool live = i < L;
@@ -210,9 +212,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         float aJ[3];
 #pragma unroll
         for (int J = 0; J < 3; ++J) aJ[J] = __expf(fminf(Gi - Gf[16 * J + 15], 0.f));
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            if (half == 1 && (warp & 1) == 0) {
+        {
+            const int half = ch_half;
+            if (half == 1 && (wq & 1) == 0) {
                 // rows 0..31: columns 32..63 lie above the diagonal.  A's upper triangle is never
                 // read; the Aqk operand needs explicit zeros there.
                 if (qk) {
@@ -225,10 +227,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                             make_uint4(0, 0, 0, 0);
                     }
                 }
-                continue;
-            }
+            } else {
             float d[32];
-            tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 32 * half, d);
+            tmem_ld32(tmem + ((uint32_t)(32 * wq) << 16) + 32 * half, d);
             GDN_PH_ACC_T(dbg, 96, 10, tq3);
             // v[c] = masked, decayed value of column 32*half + c (row scale beta_i for A rows)
             float v[32];
@@ -270,6 +271,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                 }
             }
             GDN_PH_ACC_T(dbg, 96, 11, tq3);
+            }
         }
         if (tid < 64) *reinterpret_cast<float4*>(p.g4 + (row0 + tid) * 4) = make_float4(Gf[tid], Es[tid], Bs[tid], 0.f);
     }
@@ -278,8 +280,8 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
 
     GDN_PH_ACC(dbg, 2, tp);
     // ---- 4. T = (I + A)^-1 ----------------------------------------------------------------
-    // 4a. diagonal 16x16 blocks: warp w inverts block w, lanes 0..15 each own one column.
-    {
+    // 4a. diagonal 16x16 blocks: warp w (< 4) inverts block w, lanes 0..15 each own one column.
+    if (warp < 4) {
         const int jb = warp;
         const float* Ab = Af + (16 * jb) * kFS + 16 * jb;
         if (lane < 16) {
@@ -298,9 +300,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         }
     }
     __syncthreads();
-    // 4b. off-diagonal blocks of column block jb = warp:
+    // 4b. off-diagonal blocks of column block jb = warp (< 4):
     //     T_ib,jb = -T_ib,ib * sum_{kb=jb}^{ib-1} A_ib,kb T_kb,jb   (tf32 MMAs, fp32 accumulate)
-    {
+    if (warp < 4) {
         const int jb = warp;
         float* Y = Ysc + warp * 16 * 17;
         for (int ib = jb + 1; ib < 4; ++ib) {
@@ -354,12 +356,13 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     GDN_PH_ACC(dbg, 3, tp);
     // ---- 5. MMA #2 operand [T diag(beta e^G); (T - I) diag(beta)]: bf16 [128][64] SW128 -----
     {
-        const int r = tid, m = r & 63;
+        const int r = rr, m = r & 63;
         const bool ub = r >= 64;
         const float* Trow = Tf + m * kFS;
         unsigned char* dst = sm + kOffA + r * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * ch_half + cc;
             uint32_t pk[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -400,12 +403,12 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     GDN_PH_ACC(dbg, 5, tp);
     // ---- 7. epilogue #2: rows 0-63 -> w (bf16), rows 64-127 -> u = D + beta v (f32) ---------
     {
-        const int r = tid;
-        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+        const int r = rr;
+        const uint32_t tl = tmem + ((uint32_t)(32 * wq) << 16);
         if (r < 64) {
             // w row r -> the (now free) K tile: MMA #3's B operand and the TMA store's source
 #pragma unroll 1
-            for (int cb = 0; cb < 4; ++cb) {
+            for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
                 float d[32];
                 tmem_ld32(tl + 32 * cb, d);
 #pragma unroll
@@ -422,7 +425,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
             unsigned char* ust = sm + kOffA;  // f32 staging tile of u (4 SW128 atoms of 32 columns)
             unsigned char* vt = sm + kOffV0;
 #pragma unroll 1
-            for (int cb = 0; cb < 4; ++cb) {
+            for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
                 float d[32];
                 tmem_ld32(tl + 128 + 32 * cb, d);
 #pragma unroll
@@ -472,13 +475,13 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     GDN_PH_ACC(dbg, 7, tp);
     // ---- 9. epilogue #3: rows 0-63 -> Q' = e^G q - Aqk w, rows 64-127 -> oi = Aqk u (bf16) --------
     {
-        const int r = tid;
-        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+        const int r = rr;
+        const uint32_t tl = tmem + ((uint32_t)(32 * wq) << 16);
         const int m = r & 63;
         const float eg = Es[m];
         unsigned char* dst = sm + (r < 64 ? kOffK0 : kOffV0);  // Q' -> K tile, oi -> V tile (SW128)
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {
+        for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
             float d[32];
             tmem_ld32(tl + (r < 64 ? 0 : 128) + 32 * cb, d);
 #pragma unroll
