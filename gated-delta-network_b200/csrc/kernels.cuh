@@ -47,9 +47,9 @@ struct PrefillArgs {
     int* chunk_base;       // [N+1] first slot of each sequence (prefix sum of its chunk counts)
     int* chunk_seq;        // [S]   sequence owning each slot, -1 for unused slots
     uint16_t* w;           // [8][S*64][128] bf16   w = T diag(beta e^G) K
-    float* u;              // [8][S*64][128] f32    u = beta v + (T - I) diag(beta) V
+    float* u;              // [8][S][16][64][8] f32 u = beta v + (T - I) diag(beta) V, column-group major
     uint16_t* qp;          // [8][S*64][128] bf16   Q' = diag(e^G) Q - Aqk w  (output operand)
-    uint16_t* oi;          // [8][S*64][128] bf16   oi = Aqk u                 (intra-chunk output)
+    uint16_t* oi;          // [8][S][16][64][8] bf16 oi = Aqk u (intra-chunk output), column-group major
     float* g4;             // [8][S*64][4]   f32    {G, e^G, beta, 0}
 };
 

@@ -103,12 +103,10 @@ bool map3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t d0
 
 }  // namespace
 
-bool build_prefill_maps(const PrefillArgs& p, int bv, PrefillMaps* m) {
+bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
     const uint64_t T = (uint64_t)p.T, R = (uint64_t)p.S * kChunk;
     const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
-    const auto NS = CU_TENSOR_MAP_SWIZZLE_NONE;
     // Inputs: [T][heads][128] bf16 as (col, head, token); one box = 64 columns x 1 head x 64 tokens.
     bool ok = map3d(&m->q, p.q, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
     ok = ok && map3d(&m->k, p.k, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
@@ -116,11 +114,6 @@ bool build_prefill_maps(const PrefillArgs& p, int bv, PrefillMaps* m) {
     // Workspace: [8][R][cols] as (col, row, head); one box = one 64-row chunk slot.
     ok = ok && map3d(&m->w, p.w, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
     ok = ok && map3d(&m->qp, p.qp, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
-    ok = ok && map3d(&m->oi, p.oi, BF, 128, R, kHV, 256, R * 256, (uint32_t)bv, 64, 1, NS);
-    ok = ok && map3d(&m->u, p.u, F32, 128, R, kHV, 512, R * 512, (uint32_t)bv, 64, 1, NS);
-    ok = ok && map3d(&m->g4, p.g4, F32, 4, R, kHV, 16, R * 16, 4, 64, 1, NS);
-    ok = ok && map3d(&m->u_st, p.u, F32, 128, R, kHV, 512, R * 512, 32, 64, 1, SW);
-    ok = ok && map3d(&m->oi_st, p.oi, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
     return ok;
 }
 
@@ -129,7 +122,7 @@ int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream) {
     if (!p.small_n) gdn_prefill_table_kernel<<<1, 1024, 0, stream>>>(p);
     if (p.T > 0) {
         PrefillMaps maps;
-        if (!build_prefill_maps(p, bv, &maps)) return -3;
+        if (!build_prefill_maps(p, &maps)) return -3;
         if (launch_prefill_prep(p, maps, stream) != 0) return -1;
         if (launch_prefill_scan(p, maps, bv, stream) != 0) return -1;
     } else {

@@ -17,11 +17,6 @@ struct PrefillMaps {
     CUtensorMap v;    // (128, 8, T) bf16, box 64 x 1 x 64, SWIZZLE_128B
     CUtensorMap w;    // (128 col, S*64 row, 8 head) bf16, box 64 x 64 x 1, SWIZZLE_128B
     CUtensorMap qp;   // (128, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B
-    CUtensorMap oi;   // (128, S*64, 8) bf16, box BV x 64 x 1, no swizzle
-    CUtensorMap u;    // (128, S*64, 8) f32, box BV x 64 x 1, no swizzle
-    CUtensorMap g4;   // (4, S*64, 8) f32, box 4 x 64 x 1, no swizzle
-    CUtensorMap u_st;   // (128, S*64, 8) f32, box 32 x 64 x 1, SWIZZLE_128B (prep's stores)
-    CUtensorMap oi_st;  // (128, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B (prep's stores)
 };
 
 // Sequence n's token range [s, e), clamped to [0, T] (malformed cu_seqlens cannot index outside).
@@ -69,7 +64,14 @@ __device__ __forceinline__ void warp_chunk_lookup(const PrefillArgs& p, int n, i
     *seq_out = owner ? __ffs(owner) - 1 : -1;
 }
 
-bool build_prefill_maps(const PrefillArgs& p, int bv, PrefillMaps* m);
+bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m);
+
+// Workspace element offset of column group cg (8 state columns) of chunk slot `slot`, v-head hv,
+// in the column-group-major u / oi regions: one group is a contiguous [64 rows][8] block, so a
+// scan CTA's slice of BV columns is one contiguous bulk copy.
+__host__ __device__ __forceinline__ size_t cg_off(int hv, int S, int slot, int cg) {
+    return (((size_t)hv * S + slot) * 16 + cg) * 64 * 8;
+}
 int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream);
 

@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         } else {
             const int m = r - 64;
             const float be = Bs[m];
-            unsigned char* ust = sm + kOffA;  // f32 staging tile of u (4 SW128 atoms of 32 columns)
+            unsigned char* ust = sm + kOffA;  // f32 staging of u, column-group major [16][64][8]
             unsigned char* vt = sm + kOffV0;
 #pragma unroll 1
             for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                     o.y = fmaf(be, __uint_as_float(vv.x & 0xffff0000u), d[4 * j4 + 1]);
                     o.z = fmaf(be, __uint_as_float(vv.y << 16), d[4 * j4 + 2]);
                     o.w = fmaf(be, __uint_as_float(vv.y & 0xffff0000u), d[4 * j4 + 3]);
-                    *reinterpret_cast<float4*>(ust + sw128_off_f32(m, c, 8192)) = o;
+                    *reinterpret_cast<float4*>(ust + ((c >> 3) * 64 + m) * 32 + (c & 7) * 4) = o;
                     // u (bf16) replaces this thread's own V row in place: MMA #3's B operand
                     *vp = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
                 }
@@ -455,8 +455,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         const int wr = slot * kChunk;
         tma_store_3d(&maps.w, 0, wr, hv, sm + kOffK0);
         tma_store_3d(&maps.w, 64, wr, hv, sm + kOffK1);
-#pragma unroll
-        for (int a = 0; a < 4; ++a) tma_store_3d(&maps.u_st, 32 * a, wr, hv, sm + kOffA + 8192 * a);
+        bulk_store(p.u + cg_off(hv, p.S, slot, 0), sm + kOffA, 16 * 64 * 8 * 4);
         tma_store_commit();
         tc_fence_after();
         constexpr uint32_t idesc = umma_idesc_bf16(128, 256, false, true);
@@ -479,7 +478,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         const uint32_t tl = tmem + ((uint32_t)(32 * wq) << 16);
         const int m = r & 63;
         const float eg = Es[m];
-        unsigned char* dst = sm + (r < 64 ? kOffK0 : kOffV0);  // Q' -> K tile, oi -> V tile (SW128)
+        // Q' -> K tile (SW128, TMA store); oi -> staging [16][64][8] bf16 in the (read) u staging area
 #pragma unroll 1
         for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
             float d[32];
@@ -500,9 +499,12 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
 #pragma unroll
                     for (int e = 0; e < 8; ++e) x[e] = d[8 * j8 + e];
                 }
-                *reinterpret_cast<uint4*>(dst + sw128_off(m, c, kOffK1 - kOffK0)) =
-                    make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
-                               pack_bf16x2(x[6], x[7]));
+                const uint4 x4 = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+                                            pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+                if (r < 64)
+                    *reinterpret_cast<uint4*>(sm + kOffK0 + sw128_off(m, c, kOffK1 - kOffK0)) = x4;
+                else
+                    *reinterpret_cast<uint4*>(sm + kOffA + ((c >> 3) * 64 + m) * 16) = x4;
             }
         }
     }
@@ -512,8 +514,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         const int wr = slot * kChunk;
         tma_store_3d(&maps.qp, 0, wr, hv, sm + kOffK0);
         tma_store_3d(&maps.qp, 64, wr, hv, sm + kOffK1);
-        tma_store_3d(&maps.oi_st, 0, wr, hv, sm + kOffV0);
-        tma_store_3d(&maps.oi_st, 64, wr, hv, sm + kOffV1);
+        bulk_store(p.oi + cg_off(hv, p.S, slot, 0), sm + kOffA, 16 * 64 * 8 * 2);
         tma_store_commit();
     }
 

@@ -36,8 +36,8 @@ struct Scan2Cfg {
     static constexpr uint32_t kOffW = 0;        // 2 atoms of 64 rows x 128 B (atom stride 8 KB)
     static constexpr uint32_t kOffQ = 16384;
     static constexpr uint32_t kOffK = 32768;
-    static constexpr uint32_t kOffU = 49152;                // [64][BV] f32
-    static constexpr uint32_t kOffO = kOffU + 64 * BV * 4;  // [64][BV] bf16 (oi)
+    static constexpr uint32_t kOffU = 49152;                // [BV/8][64][8] f32 (u, column-group major)
+    static constexpr uint32_t kOffO = kOffU + 64 * BV * 4;  // [BV/8][64][8] bf16 (oi)
     static constexpr uint32_t kOffG = kOffO + 64 * BV * 2;  // [64][4] f32 {G, e^G, beta, 0}
     static constexpr uint32_t kStage = ((kOffG + 1024) + 1023) & ~1023u;
     static constexpr uint32_t kTxBytes = 3 * 16384 + 64 * BV * 6 + 1024;
@@ -134,9 +134,6 @@ __global__ void __launch_bounds__(288, 1)
             tma_prefetch_desc(&maps.w);
             tma_prefetch_desc(&maps.qp);
             tma_prefetch_desc(&maps.k);
-            tma_prefetch_desc(&maps.u);
-            tma_prefetch_desc(&maps.oi);
-            tma_prefetch_desc(&maps.g4);
             for (int c = 0; c < nchunks; ++c) {
                 if (c >= C::kStages &&
                     !mbar_wait(empty + (c % C::kStages), (uint32_t)((c / C::kStages - 1) & 1), p.status,
@@ -153,9 +150,10 @@ __global__ void __launch_bounds__(288, 1)
                 tma_load_3d(st + C::kOffQ + 8192, &maps.qp, 64, wr, hv, bar);
                 tma_load_3d(st + C::kOffK, &maps.k, 0, hq, t0, bar);
                 tma_load_3d(st + C::kOffK + 8192, &maps.k, 64, hq, t0, bar);
-                tma_load_3d(st + C::kOffU, &maps.u, v0, wr, hv, bar);
-                tma_load_3d(st + C::kOffO, &maps.oi, v0, wr, hv, bar);
-                tma_load_3d(st + C::kOffG, &maps.g4, 0, wr, hv, bar);
+                const int slot = slot0 + c;
+                bulk_load(st + C::kOffU, p.u + cg_off(hv, p.S, slot, v0 / 8), 64 * BV * 4, bar);
+                bulk_load(st + C::kOffO, p.oi + cg_off(hv, p.S, slot, v0 / 8), 64 * BV * 2, bar);
+                bulk_load(st + C::kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, bar);
             }
         }
         return;
@@ -241,7 +239,7 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
                     for (int nt = 0; nt < NT8; ++nt) {
                         const int col = 8 * nt + 2 * tq;
-                        const float2 uu = *reinterpret_cast<const float2*>(Us + row * BV + col);
+                        const float2 uu = *reinterpret_cast<const float2*>(Us + (col >> 3) * 512 + row * 8 + (col & 7));
                         const float d0 = (uu.x - (pa[nt][2 * half] + pb[nt][2 * half])) * ed;
                         const float d1 = (uu.y - (pa[nt][2 * half + 1] + pb[nt][2 * half + 1])) * ed;
                         const uint32_t hi = pack_bf16x2(d0, d1);
@@ -254,7 +252,7 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
                     for (int nt = 0; nt < NT8; ++nt) {
                         const int col = 8 * nt + 2 * tq;
-                        const uint32_t oo = *reinterpret_cast<const uint32_t*>(Os + row * BV + col);
+                        const uint32_t oo = *reinterpret_cast<const uint32_t*>(Os + (col >> 3) * 512 + row * 8 + (col & 7));
                         *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16x2(
                             p.scale * (pa[nt][2 * half] + pb[nt][2 * half] + __uint_as_float(oo << 16)),
                             p.scale * (pa[nt][2 * half + 1] + pb[nt][2 * half + 1] + __uint_as_float(oo & 0xffff0000u)));

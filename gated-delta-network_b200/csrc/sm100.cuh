@@ -85,6 +85,17 @@ __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk
 __device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Wait until the committed stores are complete (written to global memory).
 __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// 1-D bulk copies (contiguous bytes; 16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -95,13 +106,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 __device__ __forceinline__ uint32_t sw128_off(int r, int c, uint32_t atom_stride) {
     return (uint32_t)(c >> 6) * atom_stride + (uint32_t)r * 128u + ((((uint32_t)(c >> 3) & 7u) ^ ((uint32_t)r & 7u)) << 4) +
            (uint32_t)(c & 7) * 2u;
-}
-
-// Byte offset of element (r, c) of a [rows][128] f32 tile stored as four 32-column
-// SWIZZLE_128B atoms (atom a = c / 32 holds rows x 128 B) of `atom_stride` bytes each.
-__device__ __forceinline__ uint32_t sw128_off_f32(int r, int c, uint32_t atom_stride) {
-    return (uint32_t)(c >> 5) * atom_stride + (uint32_t)r * 128u + ((((uint32_t)(c >> 2) & 7u) ^ ((uint32_t)r & 7u)) << 4) +
-           (uint32_t)(c & 3) * 4u;
 }
 
 // ---- tcgen05 / TMEM -------------------------------------------------------------------------
