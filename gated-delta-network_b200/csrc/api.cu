@@ -119,6 +119,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.S = lay.S;
     p.small_n = N <= gdn::kSmallN ? 1 : 0;
     p.test_withhold = (flags & GDN_FLAG_TEST_WITHHOLD_CHUNK) ? 1 : 0;
+    p.no_short = (flags & GDN_FLAG_NO_SHORT_PATH) ? 1 : 0;
     p.scale = scale;
     p.out = static_cast<uint16_t*>(out);
     p.new_state = new_state;

@@ -36,6 +36,8 @@ struct PrefillArgs {
     int N, T;
     int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
     int test_withhold;     // GDN_FLAG_TEST_WITHHOLD_CHUNK: the scan skips chunk 1's copies
+    int short_path;        // 1: sequences of 1..kShortLen tokens go to the recurrent short kernel
+    int no_short;          // GDN_FLAG_NO_SHORT_PATH
     int small_n;           // 1: N is small enough for each CTA to derive its chunk slots itself
                            //    (no chunk-table launch); 0: read chunk_base / chunk_seq
     float scale;

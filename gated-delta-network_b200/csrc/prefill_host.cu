@@ -117,8 +117,15 @@ bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
     return ok;
 }
 
-int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream) {
-    if (p.N <= 0) return 0;
+int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
+    if (args.N <= 0) return 0;
+    PrefillArgs p = args;
+    // Short sequences (1..kShortLen tokens) take the recurrent kernel in batches of many
+    // sequences, where its throughput wins; with few sequences the chunked kernels process the
+    // short ones off the critical path of the longest sequence, and a separate launch would only
+    // add latency.
+    p.short_path = (!p.no_short && p.N > kSmallN) ? 1 : 0;
+    if (p.short_path && p.T > 0) launch_prefill_short(p, stream);
     if (!p.small_n) gdn_prefill_table_kernel<<<1, 1024, 0, stream>>>(p);
     if (p.T > 0) {
         PrefillMaps maps;

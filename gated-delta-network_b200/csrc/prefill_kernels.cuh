@@ -40,6 +40,13 @@ __device__ __forceinline__ void seq_bounds(const void* cu, int cu64, int n, int 
 // chunk_base / chunk_seq once per call.
 constexpr int kSmallN = 32;
 
+// Sequences of at most this many tokens take the recurrent short-sequence kernel whenever it is
+// launched (PrefillArgs::short_path).  Its SIMT cost grows with the length (3 FMAs per state
+// element per token) while a chunk on the tensor-core path costs about the same for 1..64 tokens;
+// measured on B200 the recurrent path wins up to about two dozen tokens (2.3x at 6 tokens,
+// 1.3x at 16) and loses at 60.
+constexpr int kShortLen = 24;
+
 __device__ __forceinline__ int seq_nchunks(const PrefillArgs& p, int i) {
     int s, e;
     seq_bounds(p.cu, p.cu64, i, p.T, s, e);
@@ -74,5 +81,6 @@ __host__ __device__ __forceinline__ size_t cg_off(int hv, int S, int slot, int c
 }
 int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream);
+int launch_prefill_short(const PrefillArgs& p, cudaStream_t stream);
 
 }  // namespace gdn

@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     }
     int s0, e0;
     seq_bounds(p.cu, p.cu64, seq, p.T, s0, e0);
+    if (p.short_path && e0 - s0 <= kShortLen) return;  // the recurrent short kernel owns it
     const int bos = s0 + (slot - cbase) * kChunk;
     const int L = min(kChunk, e0 - bos);
     const size_t row0 = (size_t)hv * p.S * kChunk + (size_t)slot * kChunk;  // workspace row of token bos

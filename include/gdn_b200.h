@@ -46,6 +46,8 @@ enum gdn_status {
  * GDN_DEVSTATUS_SCAN_TMA_TIMEOUT in the workspace status word and returns without hanging.
  * Outputs of such a call are invalid.  Never set in production. */
 #define GDN_FLAG_TEST_WITHHOLD_CHUNK 0x1u
+/* Tuning: keep every prefill sequence on the chunked kernels (no recurrent short-sequence path). */
+#define GDN_FLAG_NO_SHORT_PATH 0x2u
 
 /* Device-side status codes written to the first int of the prefill workspace. */
 #define GDN_DEVSTATUS_OK 0

@@ -230,3 +230,22 @@ def test_prefill_bounded_wait_reports_and_recovers():
     ro, rs = _oracle(inp)
     util.check_out(util.bits(out), ro)
     util.check_state(ns.cpu().numpy(), rs)
+
+
+@pytest.mark.parametrize("lens", [[6] * 40, [1, 24, 25, 3, 200, 0, 17] * 6, [24] * 33], ids=["40x6", "mixed", "33x24"])
+def test_prefill_short_sequence_path(lens):
+    """In batches of more than 32 sequences, sequences of up to 24 tokens take the recurrent
+    short-sequence kernel and longer ones the chunked kernels, in the same call; both must match
+    the oracle, and the chunked-only route (GDN_FLAG_NO_SHORT_PATH) must agree with it."""
+    from gdn import prefill as pmod
+
+    inp = gi.prefill_inputs(lens, seed=34 + len(lens))
+    _run_and_check(inp)
+    args = util.prefill_args(inp)
+    o1, s1 = gdn.prefill.run(*args)
+    o2 = torch.empty_like(o1)
+    s2 = torch.empty_like(s1)
+    pmod._launch(*args, o2, s2, flags=2)  # GDN_FLAG_NO_SHORT_PATH
+    torch.cuda.synchronize()
+    util.check_out(util.bits(o2), util.bits(o1), atol=2e-3, rtol=2e-2)
+    util.check_state(s2.cpu().numpy(), s1.cpu().numpy(), rel_l2=1e-4)
