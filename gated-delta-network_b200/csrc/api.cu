@@ -75,7 +75,9 @@ int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* sta
     p.out = static_cast<uint16_t*>(out);
     p.new_state = new_state;
     p.B = B;
-    if (gdn::launch_decode(p, decode_variant(B, flags), static_cast<cudaStream_t>(stream)) != 0) return GDN_ERR_SIZE;
+    const int lrc = gdn::launch_decode(p, decode_variant(B, flags), static_cast<cudaStream_t>(stream));
+    if (lrc == -1) return GDN_ERR_SIZE;  // unknown tuning variant
+    if (lrc != 0) return GDN_ERR_CUDA;
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 

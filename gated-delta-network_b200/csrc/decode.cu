@@ -42,6 +42,9 @@ __global__ void __launch_bounds__(NW * 32) gdn_decode_kernel(DecodeArgs p) {
     const size_t head_off = (size_t)bh * kD * kD;
     const int row0 = slice * kRowsPerCta + warp * 4 + rsub;
 
+    // Launched as a programmatic dependent: everything above overlapped the previous kernel's
+    // tail; no input is read before that kernel has completed.
+    pdl_wait();
     // 1. Issue every state load of this thread first.
     float4 S[RPT][4];
     if (p.state != nullptr) {
@@ -57,6 +60,7 @@ __global__ void __launch_bounds__(NW * 32) gdn_decode_kernel(DecodeArgs p) {
             for (int i = 0; i < 4; ++i) S[r][i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 
+    pdl_trigger();  // the next kernel may start launching into SM slots as this grid drains
     // 2. q, k fragments (16 elements each) and the gates.
     float qf[16], kf[16];
     {
@@ -127,34 +131,24 @@ __global__ void __launch_bounds__(NW * 32) gdn_decode_kernel(DecodeArgs p) {
     }
 }
 
+template <int NW, int RPT>
+static cudaError_t launch_variant(const DecodeArgs& p, int ctas, cudaStream_t stream) {
+    return launch_pdl(gdn_decode_kernel<NW, RPT>, dim3(ctas), dim3(NW * 32), 0, stream, p);
+}
+
 // Variant table: (warps per CTA, rows per thread).  Rows per CTA = 4*NW*RPT.
 int launch_decode(const DecodeArgs& p, int variant, cudaStream_t stream) {
     const int heads = p.B * kHV;
+    cudaError_t e;
     switch (variant) {
-        case 0: {  // 32 rows / CTA, 128 threads: 4 slices per head
-            gdn_decode_kernel<4, 2><<<heads * 4, 128, 0, stream>>>(p);
-            break;
-        }
-        case 1: {  // 64 rows / CTA, 128 threads
-            gdn_decode_kernel<4, 4><<<heads * 2, 128, 0, stream>>>(p);
-            break;
-        }
-        case 2: {  // 16 rows / CTA, 128 threads: 8 slices per head (small batches)
-            gdn_decode_kernel<4, 1><<<heads * 8, 128, 0, stream>>>(p);
-            break;
-        }
-        case 3: {  // 64 rows / CTA, 256 threads
-            gdn_decode_kernel<8, 2><<<heads * 2, 256, 0, stream>>>(p);
-            break;
-        }
-        case 4: {  // 128 rows / CTA, 256 threads: one CTA per head
-            gdn_decode_kernel<8, 4><<<heads, 256, 0, stream>>>(p);
-            break;
-        }
-        default:
-            return -1;
+        case 0: e = launch_variant<4, 2>(p, heads * 4, stream); break;  // 32 rows / CTA, 128 threads
+        case 1: e = launch_variant<4, 4>(p, heads * 2, stream); break;  // 64 rows / CTA, 128 threads
+        case 2: e = launch_variant<4, 1>(p, heads * 8, stream); break;  // 16 rows / CTA (small batches)
+        case 3: e = launch_variant<8, 2>(p, heads * 2, stream); break;  // 64 rows / CTA, 256 threads
+        case 4: e = launch_variant<8, 4>(p, heads, stream); break;      // 128 rows / CTA: one CTA per head
+        default: return -1;
     }
-    return 0;
+    return e == cudaSuccess ? 0 : -2;
 }
 
 }  // namespace gdn

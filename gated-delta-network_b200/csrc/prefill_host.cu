@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(1024) gdn_prefill_table_kernel(PrefillArgs p) 
     __shared__ int s_warp[32];
     __shared__ int s_total;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait();
+    pdl_trigger();
     if (tid == 0) *p.status = 0;
     int running = 0;
     for (int base = 0; base < p.N; base += 1024) {
@@ -125,8 +127,9 @@ int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
     // short ones off the critical path of the longest sequence, and a separate launch would only
     // add latency.
     p.short_path = (!p.no_short && p.N > kSmallN) ? 1 : 0;
-    if (p.short_path && p.T > 0) launch_prefill_short(p, stream);
-    if (!p.small_n) gdn_prefill_table_kernel<<<1, 1024, 0, stream>>>(p);
+    if (p.short_path && p.T > 0 && launch_prefill_short(p, stream) != 0) return -1;
+    if (!p.small_n && launch_pdl(gdn_prefill_table_kernel, dim3(1), dim3(1024), 0, stream, p) != cudaSuccess)
+        return -1;
     if (p.T > 0) {
         PrefillMaps maps;
         if (!build_prefill_maps(p, &maps)) return -3;

@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     // columns (ch_half 0 / 1).  Warp w reads TMEM lane quarter w % 4.
     const int rr = tid & 127, ch_half = tid >> 7, wq = warp & 3;
     const int slot = blockIdx.x, hv = blockIdx.y, hq = hv / (kHV / kH);
+    pdl_wait();  // inputs and the chunk table come from earlier work on the stream
     int seq, cbase;
     if (p.small_n) {
         // warp 0 finds the slot's sequence; the result is published through shared memory
@@ -144,6 +145,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         tma_load_3d(sm + kOffV0, &maps.v, 0, hv, bos, bar_load);
         tma_load_3d(sm + kOffV1, &maps.v, 64, hv, bos, bar_load);
     }
+    pdl_trigger();
     for (int i = tid; i < 64 * kFS; i += kThreads) Tf[i] = 0.f;
     if (warp == 0) tmem_alloc(tslot, kTmemCols);
     if (tid < 64) {
@@ -535,8 +537,7 @@ int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStrea
         cudaSuccess)
         return -1;
     dim3 grid((unsigned)p.S, kHV);
-    gdn_prefill_prep2_kernel<<<grid, kThreads, kSmem, stream>>>(p, maps);
-    return 0;
+    return launch_pdl(gdn_prefill_prep2_kernel, grid, dim3(kThreads), kSmem, stream, p, maps) == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace gdn

@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(288, 1)
     const int gq = lane >> 2, tq = lane & 3;
     const int v0 = blockIdx.x * BV;
     const int n = blockIdx.y / kHV, hv = blockIdx.y % kHV, hq = hv / (kHV / kH);
+    pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
+    pdl_trigger();
     int bos, eos;
     seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
     const int len = eos - bos;
@@ -326,8 +328,10 @@ static int launch_scan_bv(const PrefillArgs& p, const PrefillMaps& maps, cudaStr
         cudaSuccess)
         return -1;
     dim3 grid(kD / BV, p.N * kHV);
-    gdn_prefill_scan2_kernel<BV><<<grid, C::kThreads, C::kSmem, stream>>>(p, maps);
-    return 0;
+    return launch_pdl(gdn_prefill_scan2_kernel<BV>, grid, dim3(C::kThreads), C::kSmem, stream, p, maps) ==
+                   cudaSuccess
+               ? 0
+               : -1;
 }
 
 int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream) {

@@ -28,6 +28,8 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
     __shared__ float sg_[kShortLen], sb_[kShortLen];
 
     const int n = blockIdx.y / kHV, hv = blockIdx.y % kHV, hq = hv / (kHV / kH);
+    pdl_wait();
+    pdl_trigger();
     int bos, eos;
     seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
     const int len = eos - bos;
@@ -112,8 +114,7 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
 
 int launch_prefill_short(const PrefillArgs& p, cudaStream_t stream) {
     dim3 grid(kD / kShortRows, p.N * kHV);
-    gdn_prefill_short_kernel<<<grid, kShortRows * 8, 0, stream>>>(p);
-    return 0;
+    return launch_pdl(gdn_prefill_short_kernel, grid, dim3(kShortRows * 8), 0, stream, p) == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace gdn
