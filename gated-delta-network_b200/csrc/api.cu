@@ -95,7 +95,9 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     if (N == 0) return GDN_OK;
     if (!cu_seqlens || !new_state || !A_log || !dt_bias) return GDN_ERR_NULL;
     if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL;
-    if ((T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))) || !aligned16(new_state) ||
+    if ((T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(a) || !aligned16(b) ||
+                   !aligned16(out))) ||
+        !aligned16(new_state) ||
         (state && !aligned16(state)))
         return GDN_ERR_ALIGN;
     if (cu_is_int64 != 0 && cu_is_int64 != 1) return GDN_ERR_SIZE;

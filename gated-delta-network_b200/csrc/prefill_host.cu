@@ -103,6 +103,19 @@ bool map3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t d0
                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool map2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t d0, uint64_t d1, uint64_t stride1,
+           uint32_t b0, uint32_t b1) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {stride1};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
@@ -113,6 +126,9 @@ bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
     bool ok = map3d(&m->q, p.q, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
     ok = ok && map3d(&m->k, p.k, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
     ok = ok && map3d(&m->v, p.v, BF, 128, kHV, T, 256, 256 * kHV, 64, 1, 64, SW);
+    // Gates: [T][8] bf16 as (head, token); one box = the 8 heads of 64 tokens (1 KB).
+    ok = ok && map2d(&m->a, p.a, BF, kHV, T, 2 * kHV, kHV, 64);
+    ok = ok && map2d(&m->b, p.b, BF, kHV, T, 2 * kHV, kHV, 64);
     // Workspace: [8][R][cols] as (col, row, head); one box = one 64-row chunk slot.
     ok = ok && map3d(&m->w, p.w, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
     ok = ok && map3d(&m->qp, p.qp, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);

@@ -15,6 +15,8 @@ struct PrefillMaps {
     CUtensorMap q;    // (128 col, 4 head, T token) bf16, box 64 x 1 x 64, SWIZZLE_128B
     CUtensorMap k;    // same
     CUtensorMap v;    // (128, 8, T) bf16, box 64 x 1 x 64, SWIZZLE_128B
+    CUtensorMap a;    // (8 head, T token) bf16, box 8 x 64, no swizzle
+    CUtensorMap b;    // same
     CUtensorMap w;    // (128 col, S*64 row, 8 head) bf16, box 64 x 64 x 1, SWIZZLE_128B
     CUtensorMap qp;   // (128, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B
 };

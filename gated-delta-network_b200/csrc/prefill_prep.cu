@@ -45,14 +45,15 @@ constexpr uint32_t kOffAq = kOffT + 64 * kFS * 4;  // [Aqk; Aqk] bf16 [128][64] 
 constexpr uint32_t kSmemUsed = kOffAq + 16384;
 constexpr uint32_t kSmem = kSmemUsed + 1024;  // slack for 1024-byte alignment
 // inside the misc block
-constexpr uint32_t kOffY = 0;                  // [4 warps][16][17] f32
-constexpr uint32_t kOffG = kOffY + 4 * 16 * 17 * 4;
+constexpr uint32_t kOffTileA = 0;                 // [64 tokens][8 heads] bf16 a tile (TMA)
+constexpr uint32_t kOffTileB = 1024;             // [64][8] bf16 b tile (TMA)
+constexpr uint32_t kOffG = 2048;
 constexpr uint32_t kOffB = kOffG + 64 * 4;
 constexpr uint32_t kOffE = kOffB + 64 * 4;
 constexpr uint32_t kOffGf = kOffE + 64 * 4;    // [64] f32 final cumulative log decay
 constexpr uint32_t kOffBt = kOffGf + 64 * 4;   // [64] f32 exp(G_r(j) - G_j), r(j) = last token of j's 16-block
-constexpr uint32_t kOffBar = kOffBt + 64 * 4;  // 2 mbarriers
-constexpr uint32_t kOffSlot = kOffBar + 16;
+constexpr uint32_t kOffBar = kOffBt + 64 * 4;  // 3 mbarriers
+constexpr uint32_t kOffSlot = kOffBar + 32;
 static_assert(kOffSlot + 16 <= 8192, "misc block");
 constexpr uint32_t kTmemCols = 256;
 }  // namespace prep2
@@ -70,6 +71,22 @@ __device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// C += A B for 16 x 16 fp32 blocks in shared memory (row stride kFS), tf32 MMAs, one warp.
+// acc[nt] is the m16n8 C fragment of columns 8 nt .. 8 nt + 7.
+__device__ __forceinline__ void mma16_tf32(float (&acc)[2][4], const float* A, const float* B, int gq, int tq) {
+    using prep2::kFS;
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+        const float* As_ = A + 8 * ks;
+        const uint32_t a[4] = {to_tf32(As_[gq * kFS + tq]), to_tf32(As_[(gq + 8) * kFS + tq]),
+                               to_tf32(As_[gq * kFS + tq + 4]), to_tf32(As_[(gq + 8) * kFS + tq + 4])};
+        const float* Bm = B + (8 * ks) * kFS;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+            mma_tf32(acc[nt], a, to_tf32(Bm[tq * kFS + 8 * nt + gq]), to_tf32(Bm[(tq + 4) * kFS + 8 * nt + gq]));
+    }
+}
+
 __global__ void __launch_bounds__(prep2::kThreads, 2)
     gdn_prefill_prep2_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace prep2;
@@ -79,7 +96,6 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     float* Af = reinterpret_cast<float*>(sm + kOffA);
     float* Tf = reinterpret_cast<float*>(sm + kOffT);
     unsigned char* misc = sm + kOffMisc;
-    float* Ysc = reinterpret_cast<float*>(misc + kOffY);
     float* Gs = reinterpret_cast<float*>(misc + kOffG);
     float* Bs = reinterpret_cast<float*>(misc + kOffB);
     float* Es = reinterpret_cast<float*>(misc + kOffE);
@@ -87,6 +103,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     float* Bt = reinterpret_cast<float*>(misc + kOffBt);
     uint64_t* bar_load = reinterpret_cast<uint64_t*>(misc + kOffBar);
     uint64_t* bar_mma = bar_load + 1;
+    uint64_t* bar_gate = bar_load + 2;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(misc + kOffSlot);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -95,6 +112,13 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     // columns (ch_half 0 / 1).  Warp w reads TMEM lane quarter w % 4.
     const int rr = tid & 127, ch_half = tid >> 7, wq = warp & 3;
     const int slot = blockIdx.x, hv = blockIdx.y, hq = hv / (kHV / kH);
+    if (tid == 0) {  // descriptors are kernel parameters: fetch them while the previous kernel drains
+        tma_prefetch_desc(&maps.q);
+        tma_prefetch_desc(&maps.k);
+        tma_prefetch_desc(&maps.v);
+        tma_prefetch_desc(&maps.a);
+        tma_prefetch_desc(&maps.b);
+    }
     pdl_wait();  // inputs and the chunk table come from earlier work on the stream
     int seq, cbase;
     if (p.small_n) {
@@ -130,13 +154,18 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     const bool dbg = true;
     (void)dbg;
 
-    // ---- 1. barriers, TMA loads, TMEM, gates ------------------------------------------------
-    // Thread 0 issues the tile loads first thing; the other threads touch the barriers only
-    // after the block barrier below, by which time their initialisation is visible.
+    // ---- 1. barriers, TMA loads, TMEM -----------------------------------------------------
+    // Thread 0 issues the tile loads first thing (the small gate tiles first, on their own
+    // barrier); the other threads touch the barriers only after the block barrier below, by
+    // which time their initialisation is visible.
     if (tid == 0) {
         mbar_init(bar_load, 1);
         mbar_init(bar_mma, 1);
+        mbar_init(bar_gate, 1);
         mbar_fence_init();
+        mbar_arrive_expect_tx(bar_gate, 2 * 1024);
+        tma_load_2d(misc + kOffTileA, &maps.a, 0, bos, bar_gate);
+        tma_load_2d(misc + kOffTileB, &maps.b, 0, bos, bar_gate);
         mbar_arrive_expect_tx(bar_load, 6 * 8192);
         tma_load_3d(sm + kOffK0, &maps.k, 0, hq, bos, bar_load);
         tma_load_3d(sm + kOffK1, &maps.k, 64, hq, bos, bar_load);
@@ -145,16 +174,38 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         tma_load_3d(sm + kOffV0, &maps.v, 0, hv, bos, bar_load);
         tma_load_3d(sm + kOffV1, &maps.v, 64, hv, bos, bar_load);
     }
+    GDN_PH_ACC(dbg, 17, tp);
     pdl_trigger();
-    for (int i = tid; i < 64 * kFS; i += kThreads) Tf[i] = 0.f;
-    if (warp == 0) tmem_alloc(tslot, kTmemCols);
-    if (tid < 64) {
-        const int t = tid;
+    if (warp == 1) {
+        tmem_alloc(tslot, kTmemCols);  // off thread 0's path: the allocation takes ~1000 cycles
+    } else if (warp >= 2) {
+        // zero T's six upper 16 x 16 blocks (the inverse writes every other block)
+        for (int i = tid - 64; i < 6 * 256; i += kThreads - 64) {
+            const int b = i >> 8, e = i & 255;
+            const int bi = b < 3 ? 0 : (b < 5 ? 1 : 2);
+            const int bj = b < 3 ? b + 1 : (b < 5 ? b - 1 : 3);
+            Tf[(16 * bi + (e >> 4)) * kFS + 16 * bj + (e & 15)] = 0.f;
+        }
+    }
+    GDN_PH_ACC(dbg, 18, tp);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    GDN_PH_ACC(dbg, 12, tp);
+
+    // ---- 2. gates (warps 2-3) and MMA #1 (thread 0) in parallel -----------------------------
+    bool ok = true;
+    if (warp == 2 || warp == 3) {
+        // g, beta of token t from the a / b tiles ([64 tokens][8 heads] bf16); padded tokens
+        // (t >= L) carry g = 0, so their cumulative G repeats G_{L-1}, and beta = 0.
+        ok = mbar_wait(bar_gate, 0, p.status, kErrPrepTmaTimeout);
+        const int t = tid - 64;
         float gl = 0.f, be = 0.f;
-        if (t < L) {
-            const size_t tok = (size_t)(bos + t);
-            gl = log_decay(bf2f(p.a[tok * kHV + hv]), p.A_log[hv], p.dt_bias[hv]);
-            be = sigmoidf_(bf2f(p.b[tok * kHV + hv]));
+        if (ok && t < L) {
+            gl = log_decay(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileA)[t * kHV + hv]), p.A_log[hv],
+                           p.dt_bias[hv]);
+            be = sigmoidf_(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileB)[t * kHV + hv]));
         }
         float x = gl;
 #pragma unroll
@@ -164,37 +215,34 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         }
         Gs[t] = x;
         Bs[t] = be;
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tslot;
-    // Gs holds per-warp prefix sums; the chunk prefix adds warp 0's total to tokens 32..63.
-    // Padded tokens (t >= L) carry g = 0, so their cumulative G repeats G_{L-1}.
-    if (tid < 64) {
-        const float x = Gs[tid] + (tid >= 32 ? Gs[31] : 0.f);
+        named_bar_sync(2, 64);
+        // Gs holds per-warp prefix sums; the chunk prefix adds the first warp's total to tokens 32..63.
+        x = Gs[t] + (t >= 32 ? Gs[31] : 0.f);
         const float xr = __shfl_sync(0xffffffffu, x, (lane & 16) | 15);  // G at the end of this 16-block
-        Gf[tid] = x;
-        Es[tid] = __expf(x);
-        Bt[tid] = __expf(fminf(xr - x, 0.f));
+        Gf[t] = x;
+        Es[t] = __expf(x);
+        Bt[t] = __expf(fminf(xr - x, 0.f));
     }
-    bool ok = mbar_wait(bar_load, 0, p.status, kErrPrepTmaTimeout);
-    ok = __syncthreads_and(ok);  // also publishes Gf / Es
-    if (!ok) goto cleanup;
-
-    GDN_PH_ACC(dbg, 0, tp);
-    // ---- 2. MMA #1: [K; Q] (128 x 128) x K^T -> TMEM columns 0..63 ---------------------------
     if (tid == 0) {
-        tc_fence_after();
-        constexpr uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+        // MMA #1: [K; Q] (128 x 128) x K^T -> TMEM columns 0..63 (issued only if every tile
+        // landed, so a CTA that gives up never leaves an MMA in flight)
+        ok = mbar_wait(bar_gate, 0, p.status, kErrPrepTmaTimeout) &&
+             mbar_wait(bar_load, 0, p.status, kErrPrepTmaTimeout);
+        if (ok) {
+            tc_fence_after();
+            constexpr uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t koff = (uint32_t)(kk >> 2) * (kOffK1 - kOffK0) + (uint32_t)(kk & 3) * 32u;
-            umma_bf16(tmem, umma_desc_sw128(sbase + kOffK0 + koff, 16, 1024),
-                      umma_desc_sw128(sbase + kOffK0 + koff, 16, 1024), idesc, kk > 0);
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t koff = (uint32_t)(kk >> 2) * (kOffK1 - kOffK0) + (uint32_t)(kk & 3) * 32u;
+                umma_bf16(tmem, umma_desc_sw128(sbase + kOffK0 + koff, 16, 1024),
+                          umma_desc_sw128(sbase + kOffK0 + koff, 16, 1024), idesc, kk > 0);
+            }
+            umma_commit(bar_mma);
         }
-        umma_commit(bar_mma);
     }
+    ok = __syncthreads_and(ok);  // also publishes Gf / Es / Bt / Bs
+    if (!ok) goto cleanup;
+    GDN_PH_ACC(dbg, 0, tp);
     ok = mbar_wait(bar_mma, 0, p.status, kErrPrepMmaTimeout);
     ok = __syncthreads_and(ok);
     if (!ok) goto cleanup;
@@ -303,55 +351,75 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         }
     }
     __syncthreads();
-    // 4b. off-diagonal blocks of column block jb = warp (< 4):
-    //     T_ib,jb = -T_ib,ib * sum_{kb=jb}^{ib-1} A_ib,kb T_kb,jb   (tf32 MMAs, fp32 accumulate)
-    if (warp < 4) {
-        const int jb = warp;
-        float* Y = Ysc + warp * 16 * 17;
-        for (int ib = jb + 1; ib < 4; ++ib) {
-            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            for (int kb = jb; kb < ib; ++kb) {
+    GDN_PH_ACC(dbg, 13, tp);
+    // 4b. off-diagonal blocks, two levels of the blocked inverse (block indices 0..3, 16 rows):
+    //     level 1: T10 = -T11 (A10 T00), T32 = -T33 (A32 T22)
+    //     level 2: T_LL = -T_BR (A_LL T_TL) for the lower-left 32 x 32 quadrant, i.e.
+    //              X2j = A20 T0j + A21 T1j, X3j = A30 T0j + A31 T1j (j = 0, 1; T01 = 0),
+    //              T2j = -T22 X2j, T3j = -(T32 X2j + T33 X3j).
+    //     tf32 MMAs with fp32 accumulation.  Scratch tiles live in A's upper triangle (never read).
+    {
+        float acc[2][4];
+        auto zero = [&]() {
 #pragma unroll
-                for (int ks = 0; ks < 2; ++ks) {
-                    const float* As_ = Af + (16 * ib) * kFS + 16 * kb + 8 * ks;
-                    const uint32_t a[4] = {to_tf32(As_[gq * kFS + tq]), to_tf32(As_[(gq + 8) * kFS + tq]),
-                                           to_tf32(As_[gq * kFS + tq + 4]), to_tf32(As_[(gq + 8) * kFS + tq + 4])};
-                    const float* Bm = Tf + (16 * kb + 8 * ks) * kFS + 16 * jb;
+            for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-                        mma_tf32(acc[nt], a, to_tf32(Bm[tq * kFS + 8 * nt + gq]),
-                                 to_tf32(Bm[(tq + 4) * kFS + 8 * nt + gq]));
-                }
-            }
+                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+        };
+        auto blk = [&](float* base, int bi, int bj) { return base + (16 * bi) * kFS + 16 * bj; };
+        auto store = [&](float* dst, float sgn) {
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
-                Y[gq * 17 + 8 * nt + 2 * tq] = acc[nt][0];
-                Y[gq * 17 + 8 * nt + 2 * tq + 1] = acc[nt][1];
-                Y[(gq + 8) * 17 + 8 * nt + 2 * tq] = acc[nt][2];
-                Y[(gq + 8) * 17 + 8 * nt + 2 * tq + 1] = acc[nt][3];
+                dst[gq * kFS + 8 * nt + 2 * tq] = sgn * acc[nt][0];
+                dst[gq * kFS + 8 * nt + 2 * tq + 1] = sgn * acc[nt][1];
+                dst[(gq + 8) * kFS + 8 * nt + 2 * tq] = sgn * acc[nt][2];
+                dst[(gq + 8) * kFS + 8 * nt + 2 * tq + 1] = sgn * acc[nt][3];
             }
+        };
+        float* Y0 = blk(Af, 0, 1);   // level-1 product of warp 0
+        float* Y1 = blk(Af, 0, 2);   // level-1 product of warp 1
+        float* X20 = blk(Af, 0, 3);
+        float* X21 = blk(Af, 1, 2);
+        float* X30 = blk(Af, 1, 3);
+        float* X31 = blk(Af, 2, 3);
+        // level 1, plus the level-2 terms that only need the diagonal blocks
+        if (warp < 2) {
+            const int i = warp == 0 ? 1 : 3, j = i - 1;
+            float* Y = warp == 0 ? Y0 : Y1;
+            zero();
+            mma16_tf32(acc, blk(Af, i, j), blk(Tf, j, j), gq, tq);
+            store(Y, 1.f);
             __syncwarp();
-            float rr[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            const float* Dm = Tf + (16 * ib) * kFS + 16 * ib;
-#pragma unroll
-            for (int ks = 0; ks < 2; ++ks) {
-                const uint32_t a[4] = {to_tf32(Dm[gq * kFS + 8 * ks + tq]), to_tf32(Dm[(gq + 8) * kFS + 8 * ks + tq]),
-                                       to_tf32(Dm[gq * kFS + 8 * ks + tq + 4]),
-                                       to_tf32(Dm[(gq + 8) * kFS + 8 * ks + tq + 4])};
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-                    mma_tf32(rr[nt], a, to_tf32(Y[(8 * ks + tq) * 17 + 8 * nt + gq]),
-                             to_tf32(Y[(8 * ks + tq + 4) * 17 + 8 * nt + gq]));
+            zero();
+            mma16_tf32(acc, blk(Tf, i, i), Y, gq, tq);
+            store(blk(Tf, i, j), -1.f);
+        } else if (warp < 4) {
+            const int i = warp;  // X21 = A21 T11, X31 = A31 T11
+            zero();
+            mma16_tf32(acc, blk(Af, i, 1), blk(Tf, 1, 1), gq, tq);
+            store(i == 2 ? X21 : X31, 1.f);
+        } else if (warp < 6) {
+            zero();
+            mma16_tf32(acc, blk(Af, warp - 2, 0), blk(Tf, 0, 0), gq, tq);  // A20 T00 / A30 T00
+        }
+        __syncthreads();  // T10, T32, X21, X31 visible
+        if (warp == 4 || warp == 5) {
+            const int i = warp - 2;
+            mma16_tf32(acc, blk(Af, i, 1), blk(Tf, 1, 0), gq, tq);  // + A21 T10 / A31 T10
+            store(i == 2 ? X20 : X30, 1.f);
+        }
+        __syncthreads();  // X20, X30 visible
+        if (warp < 4) {
+            const int i = 2 + (warp >> 1), j = warp & 1;
+            const float* X2 = j == 0 ? X20 : X21;
+            zero();
+            if (i == 2) {
+                mma16_tf32(acc, blk(Tf, 2, 2), X2, gq, tq);
+            } else {
+                mma16_tf32(acc, blk(Tf, 3, 2), X2, gq, tq);
+                mma16_tf32(acc, blk(Tf, 3, 3), j == 0 ? X30 : X31, gq, tq);
             }
-            float* Tout = Tf + (16 * ib) * kFS + 16 * jb;
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                Tout[gq * kFS + 8 * nt + 2 * tq] = -rr[nt][0];
-                Tout[gq * kFS + 8 * nt + 2 * tq + 1] = -rr[nt][1];
-                Tout[(gq + 8) * kFS + 8 * nt + 2 * tq] = -rr[nt][2];
-                Tout[(gq + 8) * kFS + 8 * nt + 2 * tq + 1] = -rr[nt][3];
-            }
-            __syncwarp();
+            store(blk(Tf, i, j), -1.f);
         }
     }
     __syncthreads();
@@ -511,8 +579,10 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
             }
         }
     }
+    GDN_PH_ACC(dbg, 14, tp);
     fence_async_smem();
     __syncthreads();
+    GDN_PH_ACC(dbg, 15, tp);
     if (tid == 0) {
         const int wr = slot * kChunk;
         tma_store_3d(&maps.qp, 0, wr, hv, sm + kOffK0);
@@ -524,11 +594,12 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
 cleanup:
     // Shared memory must outlive the bulk stores that read it; their global writes complete
     // before the grid does, so the scan kernel (a later launch on the stream) sees them.
+    GDN_PH_ACC(dbg, 16, tp);
     if (tid == 0) tma_store_wait_read();
     GDN_PH_ACC(dbg, 8, tp);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);  // the allocating warp
 }
 
 int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream) {

@@ -29,10 +29,14 @@ def cuda_device(t: torch.Tensor, name: str) -> torch.device:
 
 
 def as_dev(t: torch.Tensor, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
-    """Contiguous tensor of `dtype` on `device` (copies only when needed)."""
+    """Contiguous, 16-byte aligned tensor of `dtype` on `device` (copies only when needed: the
+    library reads its inputs with TMA tile copies, which need 16-byte aligned bases)."""
     if t.device != device or t.dtype != dtype:
         t = t.to(device=device, dtype=dtype)
-    return t.contiguous()
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
 
 
 def ptr(t):
