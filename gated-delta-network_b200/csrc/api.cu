@@ -75,6 +75,7 @@ int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* sta
     p.out = static_cast<uint16_t*>(out);
     p.new_state = new_state;
     p.B = B;
+    p.l2norm = (flags & GDN_FLAG_QK_L2NORM) ? 1 : 0;
     const int lrc = gdn::launch_decode(p, decode_variant(B, flags), static_cast<cudaStream_t>(stream));
     if (lrc == -1) return GDN_ERR_SIZE;  // unknown tuning variant
     if (lrc != 0) return GDN_ERR_CUDA;
@@ -124,6 +125,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.small_n = N <= gdn::kSmallN ? 1 : 0;
     p.test_withhold = (flags & GDN_FLAG_TEST_WITHHOLD_CHUNK) ? 1 : 0;
     p.no_short = (flags & GDN_FLAG_NO_SHORT_PATH) ? 1 : 0;
+    p.l2norm = (flags & GDN_FLAG_QK_L2NORM) ? 1 : 0;
     p.scale = scale;
     p.out = static_cast<uint16_t*>(out);
     p.new_state = new_state;

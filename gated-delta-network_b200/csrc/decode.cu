@@ -80,6 +80,26 @@ __global__ void __launch_bounds__(NW * 32) gdn_decode_kernel(DecodeArgs p) {
             kf[4 * i + 3] = __uint_as_float(kk.y & 0xffff0000u);
         }
     }
+    if (p.l2norm) {
+        // in-kernel L2 norm of q and k (the 8 lanes of a row group hold all 128 elements)
+        float ssq = 0.f, ssk = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            ssq = fmaf(qf[e], qf[e], ssq);
+            ssk = fmaf(kf[e], kf[e], ssk);
+        }
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) {
+            ssq += __shfl_xor_sync(0xffffffffu, ssq, off);
+            ssk += __shfl_xor_sync(0xffffffffu, ssk, off);
+        }
+        const float rq = rsqrtf(ssq + 1e-6f), rk = rsqrtf(ssk + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            qf[e] *= rq;
+            kf[e] *= rk;
+        }
+    }
     const float gl = log_decay(bf2f(p.a[bi * kHV + hv]), p.A_log[hv], p.dt_bias[hv]);
     const float g = expf(gl);
     const float beta = sigmoidf_(bf2f(p.b[bi * kHV + hv]));

@@ -20,6 +20,7 @@ struct DecodeArgs {
     uint16_t* out;         // [B, 8, 128] bf16
     float* new_state;      // [B, 8, 128, 128] f32 (may alias state)
     int B;
+    int l2norm;            // GDN_FLAG_QK_L2NORM: normalise q, k in-kernel
 };
 
 struct PrefillArgs {
@@ -38,6 +39,7 @@ struct PrefillArgs {
     int test_withhold;     // GDN_FLAG_TEST_WITHHOLD_CHUNK: the scan skips chunk 1's copies
     int short_path;        // 1: sequences of 1..kShortLen tokens go to the recurrent short kernel
     int no_short;          // GDN_FLAG_NO_SHORT_PATH
+    int l2norm;            // GDN_FLAG_QK_L2NORM: normalise q, k per token and head in-kernel
     int small_n;           // 1: N is small enough for each CTA to derive its chunk slots itself
                            //    (no chunk-table launch); 0: read chunk_base / chunk_seq
     float scale;
@@ -52,7 +54,7 @@ struct PrefillArgs {
     float* u;              // [8][S][16][64][8] f32 u = beta v + (T - I) diag(beta) V, column-group major
     uint16_t* qp;          // [8][S*64][128] bf16   Q' = diag(e^G) Q - Aqk w  (output operand)
     uint16_t* oi;          // [8][S][16][64][8] bf16 oi = Aqk u (intra-chunk output), column-group major
-    float* g4;             // [8][S*64][4]   f32    {G, e^G, beta, 0}
+    float* g4;             // [8][S*64][4]   f32    {G, e^G, beta, rk} (rk = 1 / |k| with the L2 norm, else 1)
 };
 
 // Byte offsets of the workspace regions for N sequences and T tokens.

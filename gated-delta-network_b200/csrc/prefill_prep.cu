@@ -52,7 +52,10 @@ constexpr uint32_t kOffB = kOffG + 64 * 4;
 constexpr uint32_t kOffE = kOffB + 64 * 4;
 constexpr uint32_t kOffGf = kOffE + 64 * 4;    // [64] f32 final cumulative log decay
 constexpr uint32_t kOffBt = kOffGf + 64 * 4;   // [64] f32 exp(G_r(j) - G_j), r(j) = last token of j's 16-block
-constexpr uint32_t kOffBar = kOffBt + 64 * 4;  // 3 mbarriers
+constexpr uint32_t kOffRq = kOffBt + 64 * 4;   // [64] f32 1 / |q_t| (in-kernel L2 norm), else 1
+constexpr uint32_t kOffRk = kOffRq + 64 * 4;   // [64] f32 1 / |k_t|, else 1
+constexpr uint32_t kOffWf = kOffRk + 64 * 4;   // [64] f32 beta e^G / |k| (column scale of w's operand)
+constexpr uint32_t kOffBar = kOffWf + 64 * 4;  // 3 mbarriers
 constexpr uint32_t kOffSlot = kOffBar + 32;
 static_assert(kOffSlot + 16 <= 8192, "misc block");
 constexpr uint32_t kTmemCols = 256;
@@ -101,6 +104,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     float* Es = reinterpret_cast<float*>(misc + kOffE);
     float* Gf = reinterpret_cast<float*>(misc + kOffGf);
     float* Bt = reinterpret_cast<float*>(misc + kOffBt);
+    float* Rq = reinterpret_cast<float*>(misc + kOffRq);
+    float* Rk = reinterpret_cast<float*>(misc + kOffRk);
+    float* Wf = reinterpret_cast<float*>(misc + kOffWf);
     uint64_t* bar_load = reinterpret_cast<uint64_t*>(misc + kOffBar);
     uint64_t* bar_mma = bar_load + 1;
     uint64_t* bar_gate = bar_load + 2;
@@ -215,13 +221,43 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         }
         Gs[t] = x;
         Bs[t] = be;
+        float rq = 1.f, rk = 1.f;
+        if (p.l2norm) {
+            // in-kernel L2 norm: 1 / |q_t|, 1 / |k_t| from the tiles (16-byte chunks of a row are
+            // read in a rotated order, so the 32 rows of a warp hit different banks)
+            ok = mbar_wait(bar_load, 0, p.status, kErrPrepTmaTimeout) && ok;
+            if (ok) {
+                float ssq = 0.f, ssk = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int ch = (i + t) & 15;
+                    const uint32_t off = (uint32_t)(ch >> 3) * (kOffK1 - kOffK0) + (uint32_t)t * 128u + (uint32_t)(ch & 7) * 16u;
+                    const uint4 qq = *reinterpret_cast<const uint4*>(sm + kOffQ0 + off);
+                    const uint4 kk = *reinterpret_cast<const uint4*>(sm + kOffK0 + off);
+                    const uint32_t qw[4] = {qq.x, qq.y, qq.z, qq.w}, kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float q0 = __uint_as_float(qw[e] << 16), q1 = __uint_as_float(qw[e] & 0xffff0000u);
+                        const float k0 = __uint_as_float(kw[e] << 16), k1 = __uint_as_float(kw[e] & 0xffff0000u);
+                        ssq = fmaf(q0, q0, fmaf(q1, q1, ssq));
+                        ssk = fmaf(k0, k0, fmaf(k1, k1, ssk));
+                    }
+                }
+                rq = rsqrtf(ssq + 1e-6f);
+                rk = rsqrtf(ssk + 1e-6f);
+            }
+        }
+        Rq[t] = rq;
+        Rk[t] = rk;
         named_bar_sync(2, 64);
         // Gs holds per-warp prefix sums; the chunk prefix adds the first warp's total to tokens 32..63.
         x = Gs[t] + (t >= 32 ? Gs[31] : 0.f);
         const float xr = __shfl_sync(0xffffffffu, x, (lane & 16) | 15);  // G at the end of this 16-block
         Gf[t] = x;
-        Es[t] = __expf(x);
+        const float ex = __expf(x);
+        Es[t] = ex;
         Bt[t] = __expf(fminf(xr - x, 0.f));
+        Wf[t] = be * ex * rk;
     }
     if (tid == 0) {
         // MMA #1: [K; Q] (128 x 128) x K^T -> TMEM columns 0..63 (issued only if every tile
@@ -302,14 +338,20 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                     for (int c = 0; c < 16; ++c) v[16 * Jh + c] = 0.f;
                 }
             }
+            float rowf = 1.f;
+            if (p.l2norm) {  // k_j / |k_j| for every column, q_i / |q_i| or k_i / |k_i| for the row
+#pragma unroll
+                for (int c = 0; c < 32; ++c) v[c] *= Rk[32 * half + c];
+                rowf = qk ? Rq[i] : Rk[i];
+            }
             if (!qk) {
-                const float sc = live ? bi : 0.f;
+                const float sc = live ? bi * rowf : 0.f;
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4)
                     *reinterpret_cast<float4*>(Af + i * kFS + 32 * half + 4 * j4) =
                         make_float4(sc * v[4 * j4], sc * v[4 * j4 + 1], sc * v[4 * j4 + 2], sc * v[4 * j4 + 3]);
             } else {
-                const float sc = live ? 1.f : 0.f;
+                const float sc = live ? rowf : 0.f;
 #pragma unroll
                 for (int j8 = 0; j8 < 4; ++j8) {
                     const uint4 q4 = make_uint4(pack_bf16x2(sc * v[8 * j8], sc * v[8 * j8 + 1]),
@@ -324,7 +366,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
             GDN_PH_ACC_T(dbg, 96, 11, tq3);
             }
         }
-        if (tid < 64) *reinterpret_cast<float4*>(p.g4 + (row0 + tid) * 4) = make_float4(Gf[tid], Es[tid], Bs[tid], 0.f);
+        if (tid < 64) *reinterpret_cast<float4*>(p.g4 + (row0 + tid) * 4) = make_float4(Gf[tid], Es[tid], Bs[tid], Rk[tid]);
     }
     tc_fence_before();
     __syncthreads();
@@ -443,8 +485,8 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                     t0 = (j == m ? t0 - 1.f : t0) * Bs[j];
                     t1 = (j + 1 == m ? t1 - 1.f : t1) * Bs[j + 1];
                 } else {
-                    t0 *= Bs[j] * Es[j];
-                    t1 *= Bs[j + 1] * Es[j + 1];
+                    t0 *= Wf[j];
+                    t1 *= Wf[j + 1];
                 }
                 pk[e] = pack_bf16x2(t0, t1);
             }
@@ -548,7 +590,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         const int r = rr;
         const uint32_t tl = tmem + ((uint32_t)(32 * wq) << 16);
         const int m = r & 63;
-        const float eg = Es[m];
+        const float eg = Es[m] * Rq[m];
         // Q' -> K tile (SW128, TMA store); oi -> staging [16][64][8] bf16 in the (read) u staging area
 #pragma unroll 1
         for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {

@@ -238,7 +238,9 @@ __global__ void __launch_bounds__(288, 1)
             for (int half = 0; half < 2; ++half) {
                 const int row = prow0 + gq + 8 * half;
                 if (!out_warp) {
-                    const float ed = __expf(GL - G4[row * 4]);  // <= 1; padded rows have vn = 0
+                    // e^{G_L - G} <= 1 (padded rows have vn = 0), times 1 / |k| of the row's token
+                    // with the in-kernel L2 norm (K is the raw k tile), else 1
+                    const float ed = __expf(GL - G4[row * 4]) * G4[row * 4 + 3];
 #pragma unroll
                     for (int nt = 0; nt < NT8; ++nt) {
                         const int col = 8 * nt + 2 * tq;

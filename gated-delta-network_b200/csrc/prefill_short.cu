@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
     __shared__ __align__(16) uint16_t sk_[kShortLen][kD];
     __shared__ __align__(16) uint16_t sv_[kShortLen][kShortRows];
     __shared__ float sg_[kShortLen], sb_[kShortLen];
+    __shared__ float srq_[kShortLen], srk_[kShortLen];  // 1 / |q|, 1 / |k| (1 without the L2 norm)
 
     const int n = blockIdx.y / kHV, hv = blockIdx.y % kHV, hq = hv / (kHV / kH);
     pdl_wait();
@@ -66,6 +67,29 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
         sb_[t] = sigmoidf_(bf2f(p.b[g]));
     }
     __syncthreads();
+    if (p.l2norm) {
+        // in-kernel L2 norm: warp w handles tokens w, w + 4, ...; lane l sums 4 elements
+        for (int t = tid >> 5; t < len; t += (kShortRows * 8) / 32) {
+            const uint2 qq = *reinterpret_cast<const uint2*>(&sq_[t][4 * lane]);
+            const uint2 kk = *reinterpret_cast<const uint2*>(&sk_[t][4 * lane]);
+            const float q0 = __uint_as_float(qq.x << 16), q1 = __uint_as_float(qq.x & 0xffff0000u),
+                        q2 = __uint_as_float(qq.y << 16), q3 = __uint_as_float(qq.y & 0xffff0000u);
+            const float k0 = __uint_as_float(kk.x << 16), k1 = __uint_as_float(kk.x & 0xffff0000u),
+                        k2 = __uint_as_float(kk.y << 16), k3 = __uint_as_float(kk.y & 0xffff0000u);
+            float ssq = q0 * q0 + q1 * q1 + q2 * q2 + q3 * q3;
+            float ssk = k0 * k0 + k1 * k1 + k2 * k2 + k3 * k3;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                ssq += __shfl_xor_sync(0xffffffffu, ssq, off);
+                ssk += __shfl_xor_sync(0xffffffffu, ssk, off);
+            }
+            if (lane == 0) {
+                srq_[t] = rsqrtf(ssq + 1e-6f);
+                srk_[t] = rsqrtf(ssk + 1e-6f);
+            }
+        }
+        __syncthreads();
+    }
 
     for (int t = 0; t < len; ++t) {
         float qf[16], kf[16];
@@ -81,6 +105,14 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
             kf[4 * i + 1] = __uint_as_float(kk.x & 0xffff0000u);
             kf[4 * i + 2] = __uint_as_float(kk.y << 16);
             kf[4 * i + 3] = __uint_as_float(kk.y & 0xffff0000u);
+        }
+        if (p.l2norm) {
+            const float rq = srq_[t], rk = srk_[t];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                qf[e] *= rq;
+                kf[e] *= rk;
+            }
         }
         const float g = sg_[t], beta = sb_[t];
         float sk = 0.f, sq = 0.f, kq = 0.f;

@@ -15,6 +15,7 @@ _lock = threading.Lock()
 _lib = None
 
 GDN_OK = 0
+GDN_FLAG_QK_L2NORM = 0x4  # include/gdn_b200.h
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float

@@ -55,21 +55,26 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, flag
 
 
 @torch.no_grad()
-def run(q, k, v, state, A_log, a, dt_bias, b, scale):
+def run(q, k, v, state, A_log, a, dt_bias, b, scale, *, use_qk_l2norm_in_kernel=False):
     """One decode step.  Returns ``(output [B,1,8,128] bf16, new_state [B,8,128,128] fp32)``.
 
     q, k [B,1,4,128] bf16; v [B,1,8,128] bf16; state [B,8,128,128] fp32 (k-last) or None (zeros);
     A_log, dt_bias [8] fp32; a, b [B,1,8] bf16; scale float, 0-d tensor, or None/0 (1/sqrt(128)).
+    ``use_qk_l2norm_in_kernel=True`` (keyword only; not in the reference signature) normalises q and
+    k per token and head in-kernel, x * (sum x^2 + 1e-6)^-1/2, as the reference's decode sweep
+    kernel does (tests/bench_decode_sweep.py:43-46); by default q, k are used as given.
     """
     B = q.shape[0]
     dev = cuda_device(q, "q")
     output = torch.empty((B, 1, NUM_V_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
     new_state = torch.empty((B, NUM_V_HEADS, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
-    _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+    _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state,
+            flags=_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm_in_kernel else 0)
     return output, new_state
 
 
 @torch.no_grad()
-def kernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+def kernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, *, use_qk_l2norm_in_kernel=False):
     """Destination-passing decode: writes ``output`` and ``new_state`` (which may be ``state`` itself)."""
-    _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+    _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state,
+            flags=_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm_in_kernel else 0)

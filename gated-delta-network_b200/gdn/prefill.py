@@ -83,24 +83,30 @@ def read_status(workspace: torch.Tensor) -> int:
 
 
 @torch.no_grad()
-def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2norm_in_kernel=False):
     """Varlen prefill.  Returns ``(output [T,8,128] bf16, new_state [N,8,128,128] fp32)``.
 
     q, k [T,4,128] bf16; v [T,8,128] bf16; state [N,8,128,128] fp32 or None; a, b [T,8] bf16;
     cu_seqlens [N+1] int32/int64; scale float, 0-d tensor, or None/0 (1/sqrt(128)).
     Tokens outside every sequence keep a zero output, and a zero-length sequence
     gets an all-zero final state, as in the reference oracle.
+    ``use_qk_l2norm_in_kernel=True`` (keyword only; not in the reference signature) normalises q and
+    k per token and head in-kernel, x * (sum x^2 + 1e-6)^-1/2, as the reference's decode sweep
+    kernel does (tests/bench_decode_sweep.py:43-46); by default q, k are used as given.
     """
     dev = cuda_device(q, "q")
     T = q.shape[0]
     N = cu_seqlens.shape[0] - 1
     output = torch.empty((T, NUM_V_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
     new_state = torch.empty((max(N, 0), NUM_V_HEADS, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
-    _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+    _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+            flags=_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm_in_kernel else 0)
     return output, new_state
 
 
 @torch.no_grad()
-def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):
+def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
+           use_qk_l2norm_in_kernel=False):
     """Destination-passing prefill: writes ``output`` and ``new_state`` (which may be ``state``)."""
-    _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+    _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+            flags=_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm_in_kernel else 0)

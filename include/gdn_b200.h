@@ -48,6 +48,11 @@ enum gdn_status {
 #define GDN_FLAG_TEST_WITHHOLD_CHUNK 0x1u
 /* Tuning: keep every prefill sequence on the chunked kernels (no recurrent short-sequence path). */
 #define GDN_FLAG_NO_SHORT_PATH 0x2u
+/* Variant for gdn_decode_fwd, gdn_prefill_fwd and gdn_prefill_fwd_noalloc: normalise q and k of every
+ * token and q/k head in-kernel, x * (sum x^2 + 1e-6)^-1/2 in fp32, before the step (the in-kernel L2
+ * norm of the reference's decode sweep kernel, tests/bench_decode_sweep.py:43-46, and of FLA's
+ * use_qk_l2norm_in_kernel).  Without it q and k are used as given, as the reference oracles do. */
+#define GDN_FLAG_QK_L2NORM 0x4u
 
 /* Device-side status codes written to the first int of the prefill workspace. */
 #define GDN_DEVSTATUS_OK 0

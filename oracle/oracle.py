@@ -44,10 +44,11 @@ def _load():
             build()
             lib = ctypes.CDLL(_LIB_PATH)
             p = ctypes.c_void_p
-            lib.gdn_oracle_decode.argtypes = [p, p, p, p, p, p, p, p, ctypes.c_float, p, p, ctypes.c_int, ctypes.c_int]
+            lib.gdn_oracle_decode.argtypes = [p, p, p, p, p, p, p, p, ctypes.c_float, p, p, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int]
             lib.gdn_oracle_decode.restype = ctypes.c_int
             lib.gdn_oracle_prefill.argtypes = [p, p, p, p, p, p, p, p, p, ctypes.c_int, ctypes.c_int, ctypes.c_float,
-                                               p, p, ctypes.c_int]
+                                               p, p, ctypes.c_int, ctypes.c_int]
             lib.gdn_oracle_prefill.restype = ctypes.c_int
             lib.gdn_oracle_max_threads.restype = ctypes.c_int
             _lib = lib
@@ -69,9 +70,10 @@ def _scale(scale):
     return float(scale)
 
 
-def decode(q, k, v, state, A_log, a, dt_bias, b, scale, threads: int = 0):
+def decode(q, k, v, state, A_log, a, dt_bias, b, scale, threads: int = 0, qk_l2norm: bool = False):
     """Decode step.  q,k [B,1,4,128] u16; v [B,1,8,128] u16; state [B,8,128,128] f32 or None;
-    a,b [B,1,8] u16.  Returns (out [B,1,8,128] u16 bf16 bits, new_state [B,8,128,128] f32)."""
+    a,b [B,1,8] u16.  Returns (out [B,1,8,128] u16 bf16 bits, new_state [B,8,128,128] f32).
+    qk_l2norm: normalise q, k per token and head first (the in-kernel L2-norm variant)."""
     lib = _load()
     B = int(q.shape[0])
     keep = []
@@ -87,15 +89,16 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale, threads: int = 0):
     out = np.zeros((B, 1, HV, D), np.uint16)
     new_state = np.zeros((B, HV, D, D), np.float32)
     rc = lib.gdn_oracle_decode(*args, _scale(scale), out.ctypes.data_as(ctypes.c_void_p),
-                               new_state.ctypes.data_as(ctypes.c_void_p), B, int(threads))
+                               new_state.ctypes.data_as(ctypes.c_void_p), B, int(threads), int(bool(qk_l2norm)))
     if rc != 0:
         raise ValueError(f"gdn_oracle_decode failed ({rc})")
     return out, new_state
 
 
-def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: int = 0):
+def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: int = 0, qk_l2norm: bool = False):
     """Varlen prefill.  q,k [T,4,128] u16; v [T,8,128] u16; state [N,8,128,128] f32 or None;
-    a,b [T,8] u16; cu_seqlens [N+1] int.  Returns (out [T,8,128] u16, new_state [N,8,128,128] f32)."""
+    a,b [T,8] u16; cu_seqlens [N+1] int.  Returns (out [T,8,128] u16, new_state [N,8,128,128] f32).
+    qk_l2norm: normalise q, k per token and head first (the in-kernel L2-norm variant)."""
     lib = _load()
     T = int(q.shape[0])
     cu = np.ascontiguousarray(np.asarray(cu_seqlens).astype(np.int64))
@@ -114,7 +117,7 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
     new_state = np.zeros((max(N, 0), HV, D, D), np.float32)
     rc = lib.gdn_oracle_prefill(*args, cu.ctypes.data_as(ctypes.c_void_p), N, T, _scale(scale),
                                 out.ctypes.data_as(ctypes.c_void_p), new_state.ctypes.data_as(ctypes.c_void_p),
-                                int(threads))
+                                int(threads), int(bool(qk_l2norm)))
     if rc != 0:
         raise ValueError(f"gdn_oracle_prefill failed ({rc})")
     return out, new_state

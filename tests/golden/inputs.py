@@ -41,10 +41,12 @@ def gates_params(rng):
     return A_log, dt_bias
 
 
-def decode_inputs(B: int, seed: int = 0, with_state: bool = True):
+def decode_inputs(B: int, seed: int = 0, with_state: bool = True, normalized: bool = True):
+    """normalized=False leaves q, k as raw N(0,1) (inputs of the in-kernel L2-norm variant)."""
     rng = np.random.default_rng(seed)
-    q = to_bf16_bits(_l2n(_normal(rng, (B, 1, H, D))))
-    k = to_bf16_bits(_l2n(_normal(rng, (B, 1, H, D))))
+    nq = _l2n if normalized else (lambda x: x)
+    q = to_bf16_bits(nq(_normal(rng, (B, 1, H, D))))
+    k = to_bf16_bits(nq(_normal(rng, (B, 1, H, D))))
     v = to_bf16_bits(_normal(rng, (B, 1, HV, D)))
     a = to_bf16_bits(_normal(rng, (B, 1, HV)))
     b = to_bf16_bits(_normal(rng, (B, 1, HV)))
@@ -53,13 +55,15 @@ def decode_inputs(B: int, seed: int = 0, with_state: bool = True):
     return dict(q=q, k=k, v=v, state=state, A_log=A_log, a=a, dt_bias=dt_bias, b=b, scale=1.0 / math.sqrt(D))
 
 
-def prefill_inputs(lens, seed: int = 0, with_state: bool = True):
+def prefill_inputs(lens, seed: int = 0, with_state: bool = True, normalized: bool = True):
+    """normalized=False leaves q, k as raw N(0,1) (inputs of the in-kernel L2-norm variant)."""
     rng = np.random.default_rng(seed)
     lens = [int(x) for x in lens]
     T = int(sum(lens))
     N = len(lens)
-    q = to_bf16_bits(_l2n(_normal(rng, (T, H, D))))
-    k = to_bf16_bits(_l2n(_normal(rng, (T, H, D))))
+    nq = _l2n if normalized else (lambda x: x)
+    q = to_bf16_bits(nq(_normal(rng, (T, H, D))))
+    k = to_bf16_bits(nq(_normal(rng, (T, H, D))))
     v = to_bf16_bits(_normal(rng, (T, HV, D)))
     a = to_bf16_bits(_normal(rng, (T, HV)))
     b = to_bf16_bits(_normal(rng, (T, HV)))
