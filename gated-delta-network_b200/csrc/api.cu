@@ -33,17 +33,21 @@ int check_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Head size 128; any number of q/k heads H with HV a multiple of H (grouped v-heads).  The
+// reference asserts H = 4, HV = 8 (reference/gdn_decode_ref.py:32-36); other counts are a
+// superset (e.g. the qk16_v32 family).  Prefill also needs HV a multiple of 8 (its gate
+// tiles are TMA boxes of 8 heads).
 bool shape_ok(int H, int HV, int K, int V) {
-    return H == GDN_NUM_QK_HEADS && HV == GDN_NUM_V_HEADS && K == GDN_HEAD_DIM && V == GDN_HEAD_DIM;
+    return H >= 1 && H <= GDN_MAX_QK_HEADS && HV >= H && HV <= GDN_MAX_V_HEADS && HV % H == 0 && K == GDN_HEAD_DIM &&
+           V == GDN_HEAD_DIM;
 }
+bool prefill_shape_ok(int H, int HV, int K, int V) { return shape_ok(H, HV, K, V) && HV % 8 == 0; }
 
-int decode_variant(int B, unsigned flags) {
+int decode_variant(int B, int HV, unsigned flags) {
     const unsigned forced = (flags >> 8) & 0xffu;  // tuning override: variant + 1
     if (forced) return (int)forced - 1;
-    // 8 heads per batch element; keep >= ~2 CTAs per SM in flight.
-    if (B <= 8) return 2;
-    if (B <= 32) return 0;
-    return 0;
+    // small batches: 16-row CTAs keep >= ~2 CTAs per SM in flight
+    return B * HV <= 64 ? 2 : 0;
 }
 
 }  // namespace
@@ -75,23 +79,25 @@ int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* sta
     p.out = static_cast<uint16_t*>(out);
     p.new_state = new_state;
     p.B = B;
+    p.H = H;
+    p.HV = HV;
     p.l2norm = (flags & GDN_FLAG_QK_L2NORM) ? 1 : 0;
-    const int lrc = gdn::launch_decode(p, decode_variant(B, flags), static_cast<cudaStream_t>(stream));
+    const int lrc = gdn::launch_decode(p, decode_variant(B, HV, flags), static_cast<cudaStream_t>(stream));
     if (lrc == -1) return GDN_ERR_SIZE;  // unknown tuning variant
     if (lrc != 0) return GDN_ERR_CUDA;
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
 size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV, int K, int V) {
-    if (!shape_ok(H, HV, K, V) || N < 0 || T < 0) return 0;
-    return gdn::prefill_layout(N, T).total;
+    if (!prefill_shape_ok(H, HV, K, V) || N < 0 || T < 0) return 0;
+    return gdn::prefill_layout(N, T, HV).total;
 }
 
 int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state, const float* A_log,
                     const void* a, const float* dt_bias, const void* b, const void* cu_seqlens, int cu_is_int64,
                     int N, int T, float scale, void* out, float* new_state, void* workspace, size_t workspace_bytes,
                     int H, int HV, int K, int V, void* stream, unsigned flags) {
-    if (!shape_ok(H, HV, K, V)) return GDN_ERR_SHAPE;
+    if (!prefill_shape_ok(H, HV, K, V)) return GDN_ERR_SHAPE;
     if (N < 0 || T < 0) return GDN_ERR_SIZE;
     if (N == 0) return GDN_OK;
     if (!cu_seqlens || !new_state || !A_log || !dt_bias) return GDN_ERR_NULL;
@@ -102,7 +108,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
         (state && !aligned16(state)))
         return GDN_ERR_ALIGN;
     if (cu_is_int64 != 0 && cu_is_int64 != 1) return GDN_ERR_SIZE;
-    const gdn::PrefillLayout lay = gdn::prefill_layout(N, T);
+    const gdn::PrefillLayout lay = gdn::prefill_layout(N, T, HV);
     if (!workspace || workspace_bytes < lay.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return GDN_ERR_WORKSPACE;
     int rc = check_device();
@@ -121,6 +127,8 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.cu64 = cu_is_int64;
     p.N = N;
     p.T = T;
+    p.H = H;
+    p.HV = HV;
     p.S = lay.S;
     p.small_n = N <= gdn::kSmallN ? 1 : 0;
     p.test_withhold = (flags & GDN_FLAG_TEST_WITHHOLD_CHUNK) ? 1 : 0;
@@ -138,7 +146,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.oi = reinterpret_cast<uint16_t*>(ws + lay.off_oi);
     p.g4 = reinterpret_cast<float*>(ws + lay.off_g4);
     const unsigned forced_bv = (flags >> 8) & 0xffu;
-    const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N);
+    const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N, HV);
     if (bv != 8 && bv != 16 && bv != 32) return GDN_ERR_SIZE;
     if (gdn::launch_prefill(p, bv, static_cast<cudaStream_t>(stream)) != 0) return GDN_ERR_CUDA;
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
@@ -148,7 +156,7 @@ const char* gdn_status_string(int status) {
     switch (status) {
         case GDN_OK: return "ok";
         case GDN_ERR_NULL: return "a required pointer is NULL";
-        case GDN_ERR_SHAPE: return "unsupported shape (need H=4, HV=8, K=V=128)";
+        case GDN_ERR_SHAPE: return "unsupported shape (need K=V=128, HV a multiple of H; prefill: HV a multiple of 8)";
         case GDN_ERR_ALIGN: return "a tensor pointer is not 16-byte aligned";
         case GDN_ERR_SIZE: return "invalid size or option";
         case GDN_ERR_WORKSPACE: return "workspace missing, misaligned (256 B) or too small";

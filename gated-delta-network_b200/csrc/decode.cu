@@ -35,9 +35,16 @@ __global__ void __launch_bounds__(NW * 32) gdn_decode_kernel(DecodeArgs p) {
     const int rsub = lane >> 3; // row inside the warp's 4-row group
     const int slice = blockIdx.x % kSlices;
     const int bh = blockIdx.x / kSlices;
-    const int bi = bh / kHV;
-    const int hv = bh % kHV;
-    const int hq = hv / (kHV / kH);
+    int bi, hv, hq;
+    if (p.HV == kHV && p.H == kH) {  // the reference's 4 / 8 family: shifts, no divisions
+        bi = bh / kHV;
+        hv = bh % kHV;
+        hq = hv / (kHV / kH);
+    } else {
+        bi = bh / p.HV;
+        hv = bh % p.HV;
+        hq = hv / (p.HV / p.H);
+    }
 
     const size_t head_off = (size_t)bh * kD * kD;
     const int row0 = slice * kRowsPerCta + warp * 4 + rsub;
@@ -64,8 +71,8 @@ __global__ void __launch_bounds__(NW * 32) gdn_decode_kernel(DecodeArgs p) {
     // 2. q, k fragments (16 elements each) and the gates.
     float qf[16], kf[16];
     {
-        const uint16_t* qp = p.q + ((size_t)bi * kH + hq) * kD + 4 * j;
-        const uint16_t* kp = p.k + ((size_t)bi * kH + hq) * kD + 4 * j;
+        const uint16_t* qp = p.q + ((size_t)bi * p.H + hq) * kD + 4 * j;
+        const uint16_t* kp = p.k + ((size_t)bi * p.H + hq) * kD + 4 * j;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint2 qq = ld_nc_u2(qp + 32 * i);
@@ -100,9 +107,9 @@ __global__ void __launch_bounds__(NW * 32) gdn_decode_kernel(DecodeArgs p) {
             kf[e] *= rk;
         }
     }
-    const float gl = log_decay(bf2f(p.a[bi * kHV + hv]), p.A_log[hv], p.dt_bias[hv]);
+    const float gl = log_decay(bf2f(p.a[bi * p.HV + hv]), p.A_log[hv], p.dt_bias[hv]);
     const float g = expf(gl);
-    const float beta = sigmoidf_(bf2f(p.b[bi * kHV + hv]));
+    const float beta = sigmoidf_(bf2f(p.b[bi * p.HV + hv]));
 
     float kq = 0.f;
 #pragma unroll
@@ -158,7 +165,7 @@ static cudaError_t launch_variant(const DecodeArgs& p, int ctas, cudaStream_t st
 
 // Variant table: (warps per CTA, rows per thread).  Rows per CTA = 4*NW*RPT.
 int launch_decode(const DecodeArgs& p, int variant, cudaStream_t stream) {
-    const int heads = p.B * kHV;
+    const int heads = p.B * p.HV;
     cudaError_t e;
     switch (variant) {
         case 0: e = launch_variant<4, 2>(p, heads * 4, stream); break;  // 32 rows / CTA, 128 threads

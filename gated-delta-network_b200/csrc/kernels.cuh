@@ -20,6 +20,7 @@ struct DecodeArgs {
     uint16_t* out;         // [B, 8, 128] bf16
     float* new_state;      // [B, 8, 128, 128] f32 (may alias state)
     int B;
+    int H, HV;             // q/k heads and v heads (HV a multiple of H; 4 and 8 in the reference)
     int l2norm;            // GDN_FLAG_QK_L2NORM: normalise q, k in-kernel
 };
 
@@ -35,6 +36,7 @@ struct PrefillArgs {
     const void* cu;        // [N+1] int32 / int64
     int cu64;
     int N, T;
+    int H, HV;             // q/k heads and v heads (HV a multiple of H and of 8; 4 and 8 in the reference)
     int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
     int test_withhold;     // GDN_FLAG_TEST_WITHHOLD_CHUNK: the scan skips chunk 1's copies
     int short_path;        // 1: sequences of 1..kShortLen tokens go to the recurrent short kernel
@@ -68,7 +70,7 @@ int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream);
 // Slots: one per 64-token chunk of each sequence.  sum_n ceil(len_n / 64) <= T/64 + N, and
 // every chunk holds at least one token, so min(T/64 + N, T) slots always suffice.
 __host__ __device__ constexpr size_t prefill_up256(size_t x) { return (x + 255) & ~(size_t)255; }
-__host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T) {
+__host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T, int HV = 8) {
     PrefillLayout L{};
     long long S = (long long)T / 64 + N;
     if (S > T) S = T;
@@ -83,18 +85,18 @@ __host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T) {
     L.off_seq = o;
     o = prefill_up256(o + sizeof(int) * (size_t)S);
     L.off_w = o;
-    o = prefill_up256(o + (size_t)8 * rows * 128 * 2);
+    o = prefill_up256(o + (size_t)HV * rows * 128 * 2);
     L.off_u = o;
-    o = prefill_up256(o + (size_t)8 * rows * 128 * 4);
+    o = prefill_up256(o + (size_t)HV * rows * 128 * 4);
     L.off_qp = o;
-    o = prefill_up256(o + (size_t)8 * rows * 128 * 2);
+    o = prefill_up256(o + (size_t)HV * rows * 128 * 2);
     L.off_oi = o;
-    o = prefill_up256(o + (size_t)8 * rows * 128 * 2);
+    o = prefill_up256(o + (size_t)HV * rows * 128 * 2);
     L.off_g4 = o;
-    o = prefill_up256(o + (size_t)8 * rows * 4 * 4);
+    o = prefill_up256(o + (size_t)HV * rows * 4 * 4);
     L.total = o;
     return L;
 }
-int prefill_scan_bv(int N);
+int prefill_scan_bv(int N, int HV);
 
 }  // namespace gdn

@@ -49,6 +49,8 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
         g_scratch_addr[dev] = p;
     }
     const size_t need = gdn_prefill_workspace_bytes(N, T, H, HV, K, V);
+    if (need == 0) return GDN_ERR_SHAPE;
+    if (need > kNoAllocBytes) return GDN_ERR_SIZE;  // the array is sized for HV = 8 v-heads
     return gdn_prefill_fwd(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_is_int64, N, T, scale, out, new_state,
                            g_scratch_addr[dev], need, H, HV, K, V, stream, flags);
 }

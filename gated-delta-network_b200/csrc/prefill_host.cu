@@ -10,12 +10,12 @@
 
 namespace gdn {
 
-int prefill_scan_bv(int N) {
+int prefill_scan_bv(int N, int HV) {
     // (128 / BV) * N * 8 CTAs, one per SM (the 3-stage TMA ring fills shared memory).  Finer
     // slices only pay while they fit in one wave of 148 SMs; past that, wider slices amortise
     // the per-chunk W / Q' / K tile traffic over more state columns (measured on B200).
-    if (N * kHV * (kD / 8) <= 148) return 8;
-    if (N * kHV * (kD / 16) <= 148) return 16;
+    if (N * HV * (kD / 8) <= 148) return 8;
+    if (N * HV * (kD / 16) <= 148) return 16;
     return 32;
 }
 
@@ -123,15 +123,16 @@ bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
     const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
     // Inputs: [T][heads][128] bf16 as (col, head, token); one box = 64 columns x 1 head x 64 tokens.
-    bool ok = map3d(&m->q, p.q, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
-    ok = ok && map3d(&m->k, p.k, BF, 128, kH, T, 256, 256 * kH, 64, 1, 64, SW);
-    ok = ok && map3d(&m->v, p.v, BF, 128, kHV, T, 256, 256 * kHV, 64, 1, 64, SW);
-    // Gates: [T][8] bf16 as (head, token); one box = the 8 heads of 64 tokens (1 KB).
-    ok = ok && map2d(&m->a, p.a, BF, kHV, T, 2 * kHV, kHV, 64);
-    ok = ok && map2d(&m->b, p.b, BF, kHV, T, 2 * kHV, kHV, 64);
+    const uint64_t H = (uint64_t)p.H, HV = (uint64_t)p.HV;
+    bool ok = map3d(&m->q, p.q, BF, 128, H, T, 256, 256 * H, 64, 1, 64, SW);
+    ok = ok && map3d(&m->k, p.k, BF, 128, H, T, 256, 256 * H, 64, 1, 64, SW);
+    ok = ok && map3d(&m->v, p.v, BF, 128, HV, T, 256, 256 * HV, 64, 1, 64, SW);
+    // Gates: [T][HV] bf16 as (head, token); one box = 8 heads (the group of v-head hv) of 64 tokens (1 KB).
+    ok = ok && map2d(&m->a, p.a, BF, HV, T, 2 * HV, 8, 64);
+    ok = ok && map2d(&m->b, p.b, BF, HV, T, 2 * HV, 8, 64);
     // Workspace: [8][R][cols] as (col, row, head); one box = one 64-row chunk slot.
-    ok = ok && map3d(&m->w, p.w, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
-    ok = ok && map3d(&m->qp, p.qp, BF, 128, R, kHV, 256, R * 256, 64, 64, 1, SW);
+    ok = ok && map3d(&m->w, p.w, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
+    ok = ok && map3d(&m->qp, p.qp, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
     return ok;
 }
 

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
     // Row-per-thread epilogues: thread rr owns TMEM lane / row rr, the two warpgroups split the
     // columns (ch_half 0 / 1).  Warp w reads TMEM lane quarter w % 4.
     const int rr = tid & 127, ch_half = tid >> 7, wq = warp & 3;
-    const int slot = blockIdx.x, hv = blockIdx.y, hq = hv / (kHV / kH);
+    const int slot = blockIdx.x, hv = blockIdx.y, hq = hv / (p.HV / p.H);
     if (tid == 0) {  // descriptors are kernel parameters: fetch them while the previous kernel drains
         tma_prefetch_desc(&maps.q);
         tma_prefetch_desc(&maps.k);
@@ -170,8 +170,8 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         mbar_init(bar_gate, 1);
         mbar_fence_init();
         mbar_arrive_expect_tx(bar_gate, 2 * 1024);
-        tma_load_2d(misc + kOffTileA, &maps.a, 0, bos, bar_gate);
-        tma_load_2d(misc + kOffTileB, &maps.b, 0, bos, bar_gate);
+        tma_load_2d(misc + kOffTileA, &maps.a, hv & ~7, bos, bar_gate);
+        tma_load_2d(misc + kOffTileB, &maps.b, hv & ~7, bos, bar_gate);
         mbar_arrive_expect_tx(bar_load, 6 * 8192);
         tma_load_3d(sm + kOffK0, &maps.k, 0, hq, bos, bar_load);
         tma_load_3d(sm + kOffK1, &maps.k, 64, hq, bos, bar_load);
@@ -209,9 +209,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         const int t = tid - 64;
         float gl = 0.f, be = 0.f;
         if (ok && t < L) {
-            gl = log_decay(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileA)[t * kHV + hv]), p.A_log[hv],
+            gl = log_decay(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileA)[t * 8 + (hv & 7)]), p.A_log[hv],
                            p.dt_bias[hv]);
-            be = sigmoidf_(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileB)[t * kHV + hv]));
+            be = sigmoidf_(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileB)[t * 8 + (hv & 7)]));
         }
         float x = gl;
 #pragma unroll
@@ -649,7 +649,7 @@ int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStrea
     if (cudaFuncSetAttribute(gdn_prefill_prep2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
         cudaSuccess)
         return -1;
-    dim3 grid((unsigned)p.S, kHV);
+    dim3 grid((unsigned)p.S, (unsigned)p.HV);
     return launch_pdl(gdn_prefill_prep2_kernel, grid, dim3(kThreads), kSmem, stream, p, maps) == cudaSuccess ? 0 : -1;
 }
 

@@ -87,13 +87,13 @@ __global__ void __launch_bounds__(288, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;
     const int v0 = blockIdx.x * BV;
-    const int n = blockIdx.y / kHV, hv = blockIdx.y % kHV, hq = hv / (kHV / kH);
+    const int n = blockIdx.y / p.HV, hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
     int bos, eos;
     seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
     const int len = eos - bos;
-    float* st_out = p.new_state + ((size_t)n * kHV + hv) * kD * kD;
+    float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
 
     if (blockIdx.x == 0 && blockIdx.y == 0 && p.T > 0) {
         // Tokens outside [cu[0], cu[N]) belong to no sequence: zero output, as the reference
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(288, 1)
         seq_bounds(p.cu, p.cu64, 0, p.T, lo, tmp);
         seq_bounds(p.cu, p.cu64, p.N - 1, p.T, tmp, hi);
         hi = max(hi, lo);
-        const size_t row_words = kHV * kD / 8;
+        const size_t row_words = (size_t)p.HV * kD / 8;
         uint4* o4 = reinterpret_cast<uint4*>(p.out);
         for (size_t idx = tid; idx < (size_t)lo * row_words; idx += C::kThreads) o4[idx] = make_uint4(0, 0, 0, 0);
         for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += C::kThreads)
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(288, 1)
     const int mw = warp;
     float h[NT8][4];
     {
-        const float* st_in = p.state ? p.state + ((size_t)n * kHV + hv) * kD * kD : nullptr;
+        const float* st_in = p.state ? p.state + ((size_t)n * p.HV + hv) * kD * kD : nullptr;
 #pragma unroll
         for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(288, 1)
                             pack_bf16x2(d0 - __uint_as_float(hi << 16), d1 - __uint_as_float(hi & 0xffff0000u));
                     }
                 } else if (row < L) {
-                    uint16_t* dst = p.out + ((size_t)(t0 + row) * kHV + hv) * kD + v0;
+                    uint16_t* dst = p.out + ((size_t)(t0 + row) * p.HV + hv) * kD + v0;
 #pragma unroll
                     for (int nt = 0; nt < NT8; ++nt) {
                         const int col = 8 * nt + 2 * tq;
@@ -329,7 +329,7 @@ static int launch_scan_bv(const PrefillArgs& p, const PrefillMaps& maps, cudaStr
     if (cudaFuncSetAttribute(gdn_prefill_scan2_kernel<BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
         cudaSuccess)
         return -1;
-    dim3 grid(kD / BV, p.N * kHV);
+    dim3 grid(kD / BV, p.N * p.HV);
     return launch_pdl(gdn_prefill_scan2_kernel<BV>, grid, dim3(C::kThreads), C::kSmem, stream, p, maps) ==
                    cudaSuccess
                ? 0

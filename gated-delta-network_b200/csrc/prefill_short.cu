@@ -28,7 +28,7 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
     __shared__ float sg_[kShortLen], sb_[kShortLen];
     __shared__ float srq_[kShortLen], srk_[kShortLen];  // 1 / |q|, 1 / |k| (1 without the L2 norm)
 
-    const int n = blockIdx.y / kHV, hv = blockIdx.y % kHV, hq = hv / (kHV / kH);
+    const int n = blockIdx.y / p.HV, hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();
     pdl_trigger();
     int bos, eos;
@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
     const int tid = threadIdx.x, lane = tid & 31, j = lane & 7;
     const int r0 = blockIdx.x * kShortRows;
     const int row = r0 + (tid >> 3);  // state row (V index)
-    const size_t soff = (((size_t)n * kHV + hv) * kD + row) * kD + 4 * j;
+    const size_t soff = (((size_t)n * p.HV + hv) * kD + row) * kD + 4 * j;
 
     float4 S[4];
     if (p.state) {
@@ -52,17 +52,17 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
     // stage: 16 B per load, all issued before any use
     for (int idx = tid; idx < len * (kD / 8); idx += kShortRows * 8) {
         const int t = idx / (kD / 8), c = idx % (kD / 8);
-        const size_t g = ((size_t)(bos + t) * kH + hq) * kD + 8 * c;
+        const size_t g = ((size_t)(bos + t) * p.H + hq) * kD + 8 * c;
         *reinterpret_cast<uint4*>(&sq_[t][8 * c]) = *reinterpret_cast<const uint4*>(p.q + g);
         *reinterpret_cast<uint4*>(&sk_[t][8 * c]) = *reinterpret_cast<const uint4*>(p.k + g);
     }
     for (int idx = tid; idx < len * (kShortRows / 8); idx += kShortRows * 8) {
         const int t = idx / (kShortRows / 8), c = idx % (kShortRows / 8);
         *reinterpret_cast<uint4*>(&sv_[t][8 * c]) =
-            *reinterpret_cast<const uint4*>(p.v + ((size_t)(bos + t) * kHV + hv) * kD + r0 + 8 * c);
+            *reinterpret_cast<const uint4*>(p.v + ((size_t)(bos + t) * p.HV + hv) * kD + r0 + 8 * c);
     }
     for (int t = tid; t < len; t += kShortRows * 8) {
-        const size_t g = (size_t)(bos + t) * kHV + hv;
+        const size_t g = (size_t)(bos + t) * p.HV + hv;
         sg_[t] = expf(log_decay(bf2f(p.a[g]), p.A_log[hv], p.dt_bias[hv]));
         sb_[t] = sigmoidf_(bf2f(p.b[g]));
     }
@@ -138,14 +138,14 @@ __global__ void __launch_bounds__(kShortRows * 8) gdn_prefill_short_kernel(Prefi
             S[i].z = fmaf(g, S[i].z, vn * kf[4 * i + 2]);
             S[i].w = fmaf(g, S[i].w, vn * kf[4 * i + 3]);
         }
-        if (j == 0) p.out[((size_t)(bos + t) * kHV + hv) * kD + row] = f2bf(o);
+        if (j == 0) p.out[((size_t)(bos + t) * p.HV + hv) * kD + row] = f2bf(o);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) st_stream_f4(p.new_state + soff + 32 * i, S[i]);
 }
 
 int launch_prefill_short(const PrefillArgs& p, cudaStream_t stream) {
-    dim3 grid(kD / kShortRows, p.N * kHV);
+    dim3 grid(kD / kShortRows, p.N * p.HV);
     return launch_pdl(gdn_prefill_short_kernel, grid, dim3(kShortRows * 8), 0, stream, p) == cudaSuccess ? 0 : -1;
 }
 

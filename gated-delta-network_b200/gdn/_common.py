@@ -20,6 +20,18 @@ def resolve_scale(scale) -> float:
     return float(scale)
 
 
+def check_heads(Hq: int, Hk: int, HV: int, K: int, V: int, prefill: bool = False) -> None:
+    """The reference asserts 4 q/k heads, 8 v-heads and head size 128
+    (reference/gdn_decode_ref.py:32-36, reference/gdn_prefill_ref.py:33-36).  This library
+    accepts any head counts with HV a multiple of H (v-head hv reads q/k head hv // (HV // H)),
+    and for prefill HV a multiple of 8; the head size stays 128."""
+    assert Hk == Hq
+    assert K == HEAD_DIM and V == HEAD_DIM
+    assert 1 <= Hq <= HV and HV % Hq == 0
+    if prefill:
+        assert HV % 8 == 0
+
+
 def cuda_device(t: torch.Tensor, name: str) -> torch.device:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._common import HEAD_DIM, NUM_QK_HEADS, NUM_V_HEADS, as_dev, cuda_device, ptr, resolve_scale, stream_handle
+from ._common import HEAD_DIM, as_dev, check_heads, cuda_device, ptr, resolve_scale, stream_handle
 
 
 def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, flags=0):
@@ -20,11 +20,9 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, flag
     B, T, Hq, K = q.shape
     Hk = k.shape[2]
     HV, V = v.shape[2], v.shape[3]
-    # Same shape contract as the reference oracle (reference/gdn_decode_ref.py:32-36).
-    assert Hq == NUM_QK_HEADS
-    assert Hk == NUM_QK_HEADS
-    assert HV == NUM_V_HEADS
-    assert K == HEAD_DIM and V == HEAD_DIM
+    # Shape contract of the reference oracle (reference/gdn_decode_ref.py:32-36), widened to any
+    # head counts with HV a multiple of H.
+    check_heads(Hq, Hk, HV, K, V)
     assert T == 1
     s = resolve_scale(scale)
     q_ = as_dev(q, torch.bfloat16, dev)
@@ -35,13 +33,13 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, flag
     A_ = as_dev(A_log, torch.float32, dev)
     d_ = as_dev(dt_bias, torch.float32, dev)
     if tuple(a_.shape[-1:]) != (HV,) or a_.numel() != B * HV or b_.numel() != B * HV:
-        raise ValueError("a and b must hold [B, 1, 8] gate inputs")
+        raise ValueError(f"a and b must hold [B, 1, {HV}] gate inputs")
     if A_.numel() != HV or d_.numel() != HV:
-        raise ValueError("A_log and dt_bias must hold 8 values")
+        raise ValueError(f"A_log and dt_bias must hold {HV} values")
     st = None
     if state is not None:
         if tuple(state.shape) != (B, HV, V, K):
-            raise ValueError(f"state must be [B, 8, 128, 128], got {tuple(state.shape)}")
+            raise ValueError(f"state must be [B, {HV}, 128, 128], got {tuple(state.shape)}")
         st = as_dev(state, torch.float32, dev)
     for name, t, shape, dt in (("output", output, (B, HV * V), torch.bfloat16),
                                ("new_state", new_state, (B, HV * V * K), torch.float32)):
@@ -60,14 +58,17 @@ def run(q, k, v, state, A_log, a, dt_bias, b, scale, *, use_qk_l2norm_in_kernel=
 
     q, k [B,1,4,128] bf16; v [B,1,8,128] bf16; state [B,8,128,128] fp32 (k-last) or None (zeros);
     A_log, dt_bias [8] fp32; a, b [B,1,8] bf16; scale float, 0-d tensor, or None/0 (1/sqrt(128)).
+    Head counts: the reference's 4 q/k heads and 8 v-heads, or any H, HV with HV a multiple of H
+    (v-head hv reads q/k head hv // (HV // H)); the shapes above then read H for 4 and HV for 8.
     ``use_qk_l2norm_in_kernel=True`` (keyword only; not in the reference signature) normalises q and
     k per token and head in-kernel, x * (sum x^2 + 1e-6)^-1/2, as the reference's decode sweep
     kernel does (tests/bench_decode_sweep.py:43-46); by default q, k are used as given.
     """
     B = q.shape[0]
     dev = cuda_device(q, "q")
-    output = torch.empty((B, 1, NUM_V_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
-    new_state = torch.empty((B, NUM_V_HEADS, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
+    HV = v.shape[2]
+    output = torch.empty((B, 1, HV, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    new_state = torch.empty((B, HV, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
     _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state,
             flags=_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm_in_kernel else 0)
     return output, new_state

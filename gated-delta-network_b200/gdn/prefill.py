@@ -14,12 +14,13 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._common import HEAD_DIM, NUM_QK_HEADS, NUM_V_HEADS, as_dev, cuda_device, ptr, resolve_scale, stream_handle
+from ._common import HEAD_DIM, NUM_QK_HEADS, NUM_V_HEADS, as_dev, check_heads, cuda_device, ptr, resolve_scale, stream_handle
 
 
-def workspace_bytes(num_seqs: int, total_tokens: int) -> int:
-    return int(_lib.load().gdn_prefill_workspace_bytes(int(num_seqs), int(total_tokens), NUM_QK_HEADS,
-                                                       NUM_V_HEADS, HEAD_DIM, HEAD_DIM))
+def workspace_bytes(num_seqs: int, total_tokens: int, num_qk_heads: int = NUM_QK_HEADS,
+                    num_v_heads: int = NUM_V_HEADS) -> int:
+    return int(_lib.load().gdn_prefill_workspace_bytes(int(num_seqs), int(total_tokens), int(num_qk_heads),
+                                                       int(num_v_heads), HEAD_DIM, HEAD_DIM))
 
 
 def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, workspace=None, flags=0):
@@ -28,11 +29,9 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     Hk = k.shape[1]
     HV, V = v.shape[1], v.shape[2]
     N = cu_seqlens.shape[0] - 1
-    # Same shape contract as the reference oracle (reference/gdn_prefill_ref.py:33-36).
-    assert Hq == NUM_QK_HEADS
-    assert Hk == NUM_QK_HEADS
-    assert HV == NUM_V_HEADS
-    assert K == HEAD_DIM and V == HEAD_DIM
+    # Shape contract of the reference oracle (reference/gdn_prefill_ref.py:33-36), widened to any
+    # head counts with HV a multiple of H and of 8.
+    check_heads(Hq, Hk, HV, K, V, prefill=True)
     if N < 0:
         raise ValueError("cu_seqlens must hold at least one element")
     s = resolve_scale(scale)
@@ -48,20 +47,20 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     A_ = as_dev(A_log, torch.float32, dev)
     d_ = as_dev(dt_bias, torch.float32, dev)
     if a_.numel() != T * HV or b_.numel() != T * HV:
-        raise ValueError("a and b must hold [T, 8] gate inputs")
+        raise ValueError(f"a and b must hold [T, {HV}] gate inputs")
     if A_.numel() != HV or d_.numel() != HV:
-        raise ValueError("A_log and dt_bias must hold 8 values")
+        raise ValueError(f"A_log and dt_bias must hold {HV} values")
     st = None
     if state is not None:
         if tuple(state.shape) != (N, HV, V, K):
-            raise ValueError(f"state must be [N, 8, 128, 128], got {tuple(state.shape)}")
+            raise ValueError(f"state must be [N, {HV}, 128, 128], got {tuple(state.shape)}")
         st = as_dev(state, torch.float32, dev)
     for name, t, n, dt in (("output", output, T * HV * V, torch.bfloat16),
                            ("new_state", new_state, N * HV * V * K, torch.float32)):
         if t.device != dev or t.dtype != dt or not t.is_contiguous() or t.numel() != n:
             raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor with {n} elements")
     lib = _lib.load()
-    need = workspace_bytes(N, T)
+    need = workspace_bytes(N, T, Hq, HV)
     if workspace is None:
         ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
     else:
@@ -88,6 +87,8 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
 
     q, k [T,4,128] bf16; v [T,8,128] bf16; state [N,8,128,128] fp32 or None; a, b [T,8] bf16;
     cu_seqlens [N+1] int32/int64; scale float, 0-d tensor, or None/0 (1/sqrt(128)).
+    Head counts: the reference's 4 q/k heads and 8 v-heads, or any H, HV with HV a multiple of H and of 8
+    (v-head hv reads q/k head hv // (HV // H)); the shapes above then read H for 4 and HV for 8.
     Tokens outside every sequence keep a zero output, and a zero-length sequence
     gets an all-zero final state, as in the reference oracle.
     ``use_qk_l2norm_in_kernel=True`` (keyword only; not in the reference signature) normalises q and
@@ -97,8 +98,9 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
     dev = cuda_device(q, "q")
     T = q.shape[0]
     N = cu_seqlens.shape[0] - 1
-    output = torch.empty((T, NUM_V_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
-    new_state = torch.empty((max(N, 0), NUM_V_HEADS, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
+    HV = v.shape[1]
+    output = torch.empty((T, HV, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    new_state = torch.empty((max(N, 0), HV, HEAD_DIM, HEAD_DIM), dtype=torch.float32, device=dev)
     _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
             flags=_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm_in_kernel else 0)
     return output, new_state

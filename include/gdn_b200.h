@@ -65,6 +65,12 @@ enum gdn_status {
 #define GDN_NUM_QK_HEADS 4
 #define GDN_NUM_V_HEADS 8
 #define GDN_HEAD_DIM 128
+/* Other head counts are accepted as a superset of the reference: H q/k heads, HV v-heads with
+ * HV a multiple of H (v-head hv reads q/k head hv / (HV / H)), 1 <= H <= 64, HV <= 256; prefill
+ * also needs HV a multiple of 8.  Head size stays 128.  Layouts generalise the ones below with
+ * 4 -> H and 8 -> HV. */
+#define GDN_MAX_QK_HEADS 64
+#define GDN_MAX_V_HEADS 256
 #define GDN_CHUNK 64
 
 /*
@@ -85,7 +91,8 @@ enum gdn_status {
  *   scale     softmax-free output scale (the caller resolves None/0 to 1/sqrt(K))
  *   out       [B, HV, V]             bf16   (written)
  *   new_state [B, HV, V, K]          f32    (written; may alias `state`)
- *   H, HV, K, V must be 4, 8, 128, 128.  B may be 0 (no launch).
+ *   H, HV, K, V are 4, 8, 128, 128 in the reference (other H / HV: see GDN_MAX_QK_HEADS).
+ *   B may be 0 (no launch).
  * Pointers to q, k, v, state, out, new_state must be 16-byte aligned.
  */
 int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* state, const float* A_log,
@@ -142,7 +149,8 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
  * workspace is a fixed device array inside the library, sized for GDN_NOALLOC_MAX_TOKENS
  * packed tokens in at most GDN_NOALLOC_MAX_SEQS sequences (about 22 MB), which every GPU
  * that loads the library holds until the process exits.  T > GDN_NOALLOC_MAX_TOKENS or
- * N > GDN_NOALLOC_MAX_SEQS returns GDN_ERR_SIZE and launches nothing.
+ * N > GDN_NOALLOC_MAX_SEQS returns GDN_ERR_SIZE and launches nothing.  The array is sized for
+ * HV = 8; with more v-heads a call whose workspace would not fit also returns GDN_ERR_SIZE.
  * The call itself allocates nothing (no cudaMalloc / cudaFree).
  * The first call on each device (with that device current) looks up the array's device
  * address once; make that first call before any stream capture.

@@ -45,10 +45,10 @@ def _load():
             lib = ctypes.CDLL(_LIB_PATH)
             p = ctypes.c_void_p
             lib.gdn_oracle_decode.argtypes = [p, p, p, p, p, p, p, p, ctypes.c_float, p, p, ctypes.c_int, ctypes.c_int,
-                                              ctypes.c_int]
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int]
             lib.gdn_oracle_decode.restype = ctypes.c_int
             lib.gdn_oracle_prefill.argtypes = [p, p, p, p, p, p, p, p, p, ctypes.c_int, ctypes.c_int, ctypes.c_float,
-                                               p, p, ctypes.c_int, ctypes.c_int]
+                                               p, p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
             lib.gdn_oracle_prefill.restype = ctypes.c_int
             lib.gdn_oracle_max_threads.restype = ctypes.c_int
             _lib = lib
@@ -76,6 +76,7 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale, threads: int = 0, qk_l2n
     qk_l2norm: normalise q, k per token and head first (the in-kernel L2-norm variant)."""
     lib = _load()
     B = int(q.shape[0])
+    Hq, Hv = int(q.shape[-2]), int(v.shape[-2])
     keep = []
     args = []
     for x, dt in ((q, np.uint16), (k, np.uint16), (v, np.uint16)):
@@ -86,10 +87,10 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale, threads: int = 0, qk_l2n
         arr, ptr = _c(state, np.float32); keep.append(arr); args.append(ptr)
     for x, dt in ((A_log, np.float32), (a, np.uint16), (dt_bias, np.float32), (b, np.uint16)):
         arr, ptr = _c(x, dt); keep.append(arr); args.append(ptr)
-    out = np.zeros((B, 1, HV, D), np.uint16)
-    new_state = np.zeros((B, HV, D, D), np.float32)
+    out = np.zeros((B, 1, Hv, D), np.uint16)
+    new_state = np.zeros((B, Hv, D, D), np.float32)
     rc = lib.gdn_oracle_decode(*args, _scale(scale), out.ctypes.data_as(ctypes.c_void_p),
-                               new_state.ctypes.data_as(ctypes.c_void_p), B, int(threads), int(bool(qk_l2norm)))
+                               new_state.ctypes.data_as(ctypes.c_void_p), B, int(threads), int(bool(qk_l2norm)), Hq, Hv)
     if rc != 0:
         raise ValueError(f"gdn_oracle_decode failed ({rc})")
     return out, new_state
@@ -101,6 +102,7 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
     qk_l2norm: normalise q, k per token and head first (the in-kernel L2-norm variant)."""
     lib = _load()
     T = int(q.shape[0])
+    Hq, Hv = int(q.shape[-2]), int(v.shape[-2])
     cu = np.ascontiguousarray(np.asarray(cu_seqlens).astype(np.int64))
     N = int(cu.shape[0]) - 1
     keep = [cu]
@@ -113,11 +115,11 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
         arr, ptr = _c(state, np.float32); keep.append(arr); args.append(ptr)
     for x, dt in ((A_log, np.float32), (a, np.uint16), (dt_bias, np.float32), (b, np.uint16)):
         arr, ptr = _c(x, dt); keep.append(arr); args.append(ptr)
-    out = np.zeros((T, HV, D), np.uint16)
-    new_state = np.zeros((max(N, 0), HV, D, D), np.float32)
+    out = np.zeros((T, Hv, D), np.uint16)
+    new_state = np.zeros((max(N, 0), Hv, D, D), np.float32)
     rc = lib.gdn_oracle_prefill(*args, cu.ctypes.data_as(ctypes.c_void_p), N, T, _scale(scale),
                                 out.ctypes.data_as(ctypes.c_void_p), new_state.ctypes.data_as(ctypes.c_void_p),
-                                int(threads), int(bool(qk_l2norm)))
+                                int(threads), int(bool(qk_l2norm)), Hq, Hv)
     if rc != 0:
         raise ValueError(f"gdn_oracle_prefill failed ({rc})")
     return out, new_state

@@ -35,40 +35,42 @@ def _l2n(x):
     return x / np.sqrt((x.astype(np.float64) ** 2).sum(-1, keepdims=True)).astype(np.float32)
 
 
-def gates_params(rng):
-    A_log = (rng.random(HV) * math.log(16.0)).astype(np.float32)
-    dt_bias = _normal(rng, (HV,), 0.1)
+def gates_params(rng, hv: int = HV):
+    A_log = (rng.random(hv) * math.log(16.0)).astype(np.float32)
+    dt_bias = _normal(rng, (hv,), 0.1)
     return A_log, dt_bias
 
 
-def decode_inputs(B: int, seed: int = 0, with_state: bool = True, normalized: bool = True):
-    """normalized=False leaves q, k as raw N(0,1) (inputs of the in-kernel L2-norm variant)."""
+def decode_inputs(B: int, seed: int = 0, with_state: bool = True, normalized: bool = True, h: int = H, hv: int = HV):
+    """normalized=False leaves q, k as raw N(0,1) (inputs of the in-kernel L2-norm variant);
+    h, hv select another head-count family (the reference's is 4 / 8)."""
     rng = np.random.default_rng(seed)
     nq = _l2n if normalized else (lambda x: x)
-    q = to_bf16_bits(nq(_normal(rng, (B, 1, H, D))))
-    k = to_bf16_bits(nq(_normal(rng, (B, 1, H, D))))
-    v = to_bf16_bits(_normal(rng, (B, 1, HV, D)))
-    a = to_bf16_bits(_normal(rng, (B, 1, HV)))
-    b = to_bf16_bits(_normal(rng, (B, 1, HV)))
-    A_log, dt_bias = gates_params(rng)
-    state = _normal(rng, (B, HV, D, D), 0.02) if with_state else None
+    q = to_bf16_bits(nq(_normal(rng, (B, 1, h, D))))
+    k = to_bf16_bits(nq(_normal(rng, (B, 1, h, D))))
+    v = to_bf16_bits(_normal(rng, (B, 1, hv, D)))
+    a = to_bf16_bits(_normal(rng, (B, 1, hv)))
+    b = to_bf16_bits(_normal(rng, (B, 1, hv)))
+    A_log, dt_bias = gates_params(rng, hv)
+    state = _normal(rng, (B, hv, D, D), 0.02) if with_state else None
     return dict(q=q, k=k, v=v, state=state, A_log=A_log, a=a, dt_bias=dt_bias, b=b, scale=1.0 / math.sqrt(D))
 
 
-def prefill_inputs(lens, seed: int = 0, with_state: bool = True, normalized: bool = True):
-    """normalized=False leaves q, k as raw N(0,1) (inputs of the in-kernel L2-norm variant)."""
+def prefill_inputs(lens, seed: int = 0, with_state: bool = True, normalized: bool = True, h: int = H, hv: int = HV):
+    """normalized=False leaves q, k as raw N(0,1) (inputs of the in-kernel L2-norm variant);
+    h, hv select another head-count family (the reference's is 4 / 8)."""
     rng = np.random.default_rng(seed)
     lens = [int(x) for x in lens]
     T = int(sum(lens))
     N = len(lens)
     nq = _l2n if normalized else (lambda x: x)
-    q = to_bf16_bits(nq(_normal(rng, (T, H, D))))
-    k = to_bf16_bits(nq(_normal(rng, (T, H, D))))
-    v = to_bf16_bits(_normal(rng, (T, HV, D)))
-    a = to_bf16_bits(_normal(rng, (T, HV)))
-    b = to_bf16_bits(_normal(rng, (T, HV)))
-    A_log, dt_bias = gates_params(rng)
-    state = _normal(rng, (N, HV, D, D), 0.02) if with_state else None
+    q = to_bf16_bits(nq(_normal(rng, (T, h, D))))
+    k = to_bf16_bits(nq(_normal(rng, (T, h, D))))
+    v = to_bf16_bits(_normal(rng, (T, hv, D)))
+    a = to_bf16_bits(_normal(rng, (T, hv)))
+    b = to_bf16_bits(_normal(rng, (T, hv)))
+    A_log, dt_bias = gates_params(rng, hv)
+    state = _normal(rng, (N, hv, D, D), 0.02) if with_state else None
     cu = np.zeros(N + 1, np.int32)
     cu[1:] = np.cumsum(lens)
     return dict(q=q, k=k, v=v, state=state, A_log=A_log, a=a, dt_bias=dt_bias, b=b, cu_seqlens=cu,

@@ -46,6 +46,11 @@ def test_workspace_bytes(lib):
     assert w1 % 256 == 0
     assert ws(16, 32768) > ws(1, 8192)
     assert lib.gdn_prefill_workspace_bytes(1, 1024, 4, 8, 64, 128) == 0  # unsupported shape
+    # other head counts: HV a multiple of H and of 8; the per-head regions scale with HV
+    ws32 = lib.gdn_prefill_workspace_bytes(1, 1024, 16, 32, 128, 128)
+    assert 3.5 * w1 < ws32 < 4.5 * w1
+    assert lib.gdn_prefill_workspace_bytes(1, 1024, 4, 12, 128, 128) == 0
+    assert lib.gdn_prefill_workspace_bytes(1, 1024, 3, 8, 128, 128) == 0
     assert lib.gdn_prefill_workspace_bytes(-1, 1024, 4, 8, 128, 128) == 0
 
 
@@ -56,8 +61,10 @@ def _decode(lib, B=1, H=4, HV=8, K=128, V=128, ptrs=None, flags=0):
 
 
 def test_decode_rejects_bad_shapes_without_gpu(lib):
-    assert _decode(lib, H=2) == 2
-    assert _decode(lib, HV=16) == 2
+    assert _decode(lib, H=3) == 2  # HV must be a multiple of H
+    assert _decode(lib, H=0) == 2
+    assert _decode(lib, HV=2) == 2  # fewer v-heads than q/k heads
+    assert _decode(lib, H=128, HV=128) == 2  # above GDN_MAX_QK_HEADS
     assert _decode(lib, K=64) == 2
     assert _decode(lib, B=-1) == 4
 
@@ -74,14 +81,15 @@ def test_decode_rejects_null_and_misaligned(lib):
     assert _decode(lib, B=0, ptrs=p) == 0
 
 
-def _prefill(lib, N=1, T=64, ws=256, ws_bytes=1 << 30, state=None, cu64=0, H=4):
+def _prefill(lib, N=1, T=64, ws=256, ws_bytes=1 << 30, state=None, cu64=0, H=4, HV=8):
     a = 256
-    return lib.gdn_prefill_fwd(a, a, a, state, a, a, a, a, a, cu64, N, T, 1.0, a, a, ws, ws_bytes, H, 8, 128, 128,
+    return lib.gdn_prefill_fwd(a, a, a, state, a, a, a, a, a, cu64, N, T, 1.0, a, a, ws, ws_bytes, H, HV, 128, 128,
                                None, 0)
 
 
 def test_prefill_rejects_bad_arguments_without_gpu(lib):
-    assert _prefill(lib, H=8) == 2
+    assert _prefill(lib, H=3) == 2  # HV must be a multiple of H
+    assert _prefill(lib, HV=12) == 2  # prefill: HV a multiple of 8
     assert _prefill(lib, N=-1) == 4
     assert _prefill(lib, T=-5) == 4
     assert _prefill(lib, N=0) == 0  # nothing to do
