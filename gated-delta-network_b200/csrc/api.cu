@@ -147,7 +147,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.g4 = reinterpret_cast<float*>(ws + lay.off_g4);
     const unsigned forced_bv = (flags >> 8) & 0xffu;
     const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N, HV);
-    if (bv != 8 && bv != 16 && bv != 32) return GDN_ERR_SIZE;
+    if (bv != 8 && bv != 16 && bv != 32 && bv != 64) return GDN_ERR_SIZE;
     if (gdn::launch_prefill(p, bv, static_cast<cudaStream_t>(stream)) != 0) return GDN_ERR_CUDA;
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }

@@ -11,12 +11,15 @@
 namespace gdn {
 
 int prefill_scan_bv(int N, int HV) {
-    // (128 / BV) * N * 8 CTAs, one per SM (the 3-stage TMA ring fills shared memory).  Finer
-    // slices only pay while they fit in one wave of 148 SMs; past that, wider slices amortise
-    // the per-chunk W / Q' / K tile traffic over more state columns (measured on B200).
+    // (128 / BV) * N * HV CTAs, one per SM.  Few (sequence, v-head) pairs: the mma.sync scan with
+    // the finest slices that still fit one wave of 148 SMs (the chain of one sequence is the
+    // critical path, and its per-chunk step is shortest there).  More pairs: the tcgen05 scan
+    // with 64-column slices (returned as 64), whose per-chunk step is longer but covers 2-8x the
+    // columns, so it wins once the scan is bound by throughput (measured on B200: 4 x 2048
+    // tokens break even, 8 x 1024 is 1.6x and 64 x 4096 1.9x faster than 32-column slices).
     if (N * HV * (kD / 8) <= 148) return 8;
     if (N * HV * (kD / 16) <= 148) return 16;
-    return 32;
+    return 64;
 }
 
 // ---- chunk table ---------------------------------------------------------------------------
@@ -136,6 +139,11 @@ bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
     return ok;
 }
 
+// Slice width 64 selects the tcgen05 scan (prefill_scan_tc.cu), 8 / 16 / 32 the mma.sync scan.
+static int launch_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream) {
+    return bv == 64 ? launch_prefill_scan_tc(p, maps, stream) : launch_prefill_scan(p, maps, bv, stream);
+}
+
 int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
     if (args.N <= 0) return 0;
     PrefillArgs p = args;
@@ -151,9 +159,9 @@ int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
         PrefillMaps maps;
         if (!build_prefill_maps(p, &maps)) return -3;
         if (launch_prefill_prep(p, maps, stream) != 0) return -1;
-        if (launch_prefill_scan(p, maps, bv, stream) != 0) return -1;
+        if (launch_scan(p, maps, bv, stream) != 0) return -1;
     } else {
-        if (launch_prefill_scan(p, PrefillMaps{}, bv, stream) != 0) return -1;
+        if (launch_scan(p, PrefillMaps{}, bv, stream) != 0) return -1;
     }
     return 0;
 }

@@ -73,6 +73,21 @@ __device__ __forceinline__ void warp_chunk_lookup(const PrefillArgs& p, int n, i
     *seq_out = owner ? __ffs(owner) - 1 : -1;
 }
 
+// Warp-wide, N <= 32: the sequence with the r-th largest chunk count (ties by index).  The scan
+// maps its CTA rows through this so that the longest sequences -- the critical path of a varlen
+// batch -- are scheduled first.  Every lane returns the same value.
+__device__ __forceinline__ int warp_seq_by_rank(const PrefillArgs& p, int r) {
+    const int lane = threadIdx.x & 31;
+    const int nc = lane < p.N ? seq_nchunks(p, lane) : -1;
+    int rank = 0;
+    for (int j = 0; j < p.N; ++j) {
+        const int ncj = __shfl_sync(0xffffffffu, nc, j);
+        rank += (ncj > nc || (ncj == nc && j < lane)) ? 1 : 0;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, lane < p.N && rank == r);
+    return hit ? __ffs(hit) - 1 : r;
+}
+
 bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m);
 
 // Workspace element offset of column group cg (8 state columns) of chunk slot `slot`, v-head hv,
@@ -83,6 +98,7 @@ __host__ __device__ __forceinline__ size_t cg_off(int hv, int S, int slot, int c
 }
 int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream);
+int launch_prefill_scan_tc(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_short(const PrefillArgs& p, cudaStream_t stream);
 
 }  // namespace gdn

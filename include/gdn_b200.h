@@ -39,7 +39,8 @@ enum gdn_status {
 
 /* Flags (bitwise OR) accepted by the entry points.
  * Bits 8-15 (value << 8) force a kernel variant for tuning: the decode CTA tiling (variant + 1)
- * or the prefill scan's state-column slice width (8, 16 or 32); 0 lets the library choose. */
+ * or the prefill scan's state-column slice width (8, 16 or 32: mma.sync scan; 64: tcgen05 scan);
+ * 0 lets the library choose. */
 #define GDN_FLAG_NONE 0u
 /* Failure-detection test hook for gdn_prefill_fwd: the scan kernel withholds the TMA copies of
  * each sequence's second chunk, so its bounded wait expires (after about 2 s), the call records

@@ -135,6 +135,27 @@ def test_prefill_deterministic_and_bv_variants():
         assert torch.equal(out, o1) and torch.equal(ns, s1)
 
 
+TC_CASES = [[300, 77], [1], [64], [130, 0, 77, 300], [1000], [6] * 40 + [100, 70]]
+
+
+@pytest.mark.parametrize("lens", TC_CASES, ids=["300-77", "1", "64", "mixed4", "1000", "short42"])
+@pytest.mark.parametrize("with_state", [True, False], ids=["h0", "zero"])
+def test_prefill_tcgen05_scan_matches_oracle(lens, with_state):
+    """The tcgen05 scan (64-column slices, the default for many sequences), forced on any batch."""
+    from gdn import prefill as pmod
+
+    inp = gi.prefill_inputs(lens, seed=40 + len(lens), with_state=with_state)
+    args = util.prefill_args(inp)
+    T, N = sum(lens), len(lens)
+    out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(N, 8, 128, 128, dtype=torch.float32, device="cuda")
+    pmod._launch(*args, out, ns, flags=64 << 8)
+    torch.cuda.synchronize()
+    ro, rs = _oracle(inp)
+    util.check_out(util.bits(out), ro)
+    util.check_state(ns.cpu().numpy(), rs)
+
+
 def test_prefill_strong_decay_extremes():
     inp = gi.prefill_inputs([130, 64], seed=28)
     inp["A_log"] = np.array([np.log(16.0), 0.0, -8.0, np.log(16.0), -20.0, 2.0, 0.5, -1.0], np.float32)
@@ -210,10 +231,12 @@ def test_prefill_more_sequences_than_one_table_tile():
 
 
 @pytest.mark.timeout(120)
-def test_prefill_bounded_wait_reports_and_recovers():
+@pytest.mark.parametrize("scan", [0, 64], ids=["mma_sync_scan", "tcgen05_scan"])
+def test_prefill_bounded_wait_reports_and_recovers(scan):
     """Failure detection without a GPU fault: with the test hook the scan's producer withholds a
     chunk's TMA copies, the math warps' bounded mbarrier wait expires, the kernel records status 1
-    in the workspace and returns; the context stays usable and the next call is correct."""
+    in the workspace and returns; the context stays usable and the next call is correct.  Both
+    scan kernels (mma.sync and tcgen05) are exercised."""
     from gdn import prefill as pmod
 
     inp = gi.prefill_inputs([200], seed=33)
@@ -221,7 +244,7 @@ def test_prefill_bounded_wait_reports_and_recovers():
     out = torch.empty(200, 8, 128, dtype=torch.bfloat16, device="cuda")
     ns = torch.empty(1, 8, 128, 128, dtype=torch.float32, device="cuda")
     ws = torch.empty(gdn.prefill.workspace_bytes(1, 200), dtype=torch.uint8, device="cuda")
-    pmod._launch(*args, out, ns, workspace=ws, flags=1)  # GDN_FLAG_TEST_WITHHOLD_CHUNK
+    pmod._launch(*args, out, ns, workspace=ws, flags=1 | (scan << 8))  # GDN_FLAG_TEST_WITHHOLD_CHUNK
     torch.cuda.synchronize()
     assert gdn.prefill.read_status(ws) == 1  # GDN_DEVSTATUS_SCAN_TMA_TIMEOUT
     pmod._launch(*args, out, ns, workspace=ws)
