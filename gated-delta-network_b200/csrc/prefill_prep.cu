@@ -90,6 +90,21 @@ __device__ __forceinline__ void mma16_tf32(float (&acc)[2][4], const float* A, c
     }
 }
 
+// body(cb, d) for this thread's two 32-column TMEM blocks cb0 and cb0 + 1 (taddr0 = block cb0):
+// the second block's load is in flight while the first block is processed.
+template <typename F>
+__device__ __forceinline__ void tmem_two_blocks(uint32_t taddr0, int cb0, F&& body) {
+    uint32_t da[32], db[32];
+    tmem_ld32_async(taddr0, da);
+    tmem_ld_wait();
+    tmem_regs_ready(da);
+    tmem_ld32_async(taddr0 + 32, db);
+    body(cb0, da);
+    tmem_ld_wait();
+    tmem_regs_ready(db);
+    body(cb0 + 1, db);
+}
+
 __global__ void __launch_bounds__(prep2::kThreads, 2)
     gdn_prefill_prep2_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace prep2;
@@ -520,10 +535,8 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         const uint32_t tl = tmem + ((uint32_t)(32 * wq) << 16);
         if (r < 64) {
             // w row r -> the (now free) K tile: MMA #3's B operand and the TMA store's source
-#pragma unroll 1
-            for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
-                float d[32];
-                tmem_ld32(tl + 32 * cb, d);
+            tmem_two_blocks(tl + 64 * ch_half, 2 * ch_half, [&](int cb, const uint32_t(&dr)[32]) {
+                const float* d = reinterpret_cast<const float*>(dr);
 #pragma unroll
                 for (int j8 = 0; j8 < 4; ++j8) {
                     const uint4 w4 =
@@ -531,16 +544,14 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                                    pack_bf16x2(d[8 * j8 + 4], d[8 * j8 + 5]), pack_bf16x2(d[8 * j8 + 6], d[8 * j8 + 7]));
                     *reinterpret_cast<uint4*>(sm + kOffK0 + sw128_off(r, 32 * cb + 8 * j8, kOffK1 - kOffK0)) = w4;
                 }
-            }
+            });
         } else {
             const int m = r - 64;
             const float be = Bs[m];
             unsigned char* ust = sm + kOffA;  // f32 staging of u, column-group major [16][64][8]
             unsigned char* vt = sm + kOffV0;
-#pragma unroll 1
-            for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
-                float d[32];
-                tmem_ld32(tl + 128 + 32 * cb, d);
+            tmem_two_blocks(tl + 128 + 64 * ch_half, 2 * ch_half, [&](int cb, const uint32_t(&dr)[32]) {
+                const float* d = reinterpret_cast<const float*>(dr);
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
                     const int c = 32 * cb + 4 * j4;
@@ -555,7 +566,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                     // u (bf16) replaces this thread's own V row in place: MMA #3's B operand
                     *vp = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
                 }
-            }
+            });
         }
     }
     fence_async_smem();
@@ -592,10 +603,8 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         const int m = r & 63;
         const float eg = Es[m] * Rq[m];
         // Q' -> K tile (SW128, TMA store); oi -> staging [16][64][8] bf16 in the (read) u staging area
-#pragma unroll 1
-        for (int cb = 2 * ch_half; cb < 2 * ch_half + 2; ++cb) {
-            float d[32];
-            tmem_ld32(tl + (r < 64 ? 0 : 128) + 32 * cb, d);
+        tmem_two_blocks(tl + (r < 64 ? 0 : 128) + 64 * ch_half, 2 * ch_half, [&](int cb, const uint32_t(&dr)[32]) {
+            const float* d = reinterpret_cast<const float*>(dr);
 #pragma unroll
             for (int j8 = 0; j8 < 4; ++j8) {
                 const int c = 32 * cb + 8 * j8;
@@ -619,7 +628,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                 else
                     *reinterpret_cast<uint4*>(sm + kOffA + ((c >> 3) * 64 + m) * 16) = x4;
             }
-        }
+        });
     }
     GDN_PH_ACC(dbg, 14, tp);
     fence_async_smem();

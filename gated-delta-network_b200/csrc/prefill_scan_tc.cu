@@ -68,7 +68,8 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
     const int hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
-    const int n = blockIdx.y / p.HV;
+    // longest sequence first (N <= 32), as in prefill_scan.cu
+    const int n = p.small_n ? warp_seq_by_rank(p, blockIdx.y / p.HV) : blockIdx.y / p.HV;
     int bos, eos;
     seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
     const int len = eos - bos;
