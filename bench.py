@@ -52,7 +52,7 @@ N_STATE_BUFS = 8
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum), or None.
 # Source: the ncu summaries under profiles/ (decode B=64 launch; prefill kernels at T=8192).
 # decode: 33.83 MB read; the 33.55 MB of state writes are still dirty in L2 when ncu's replayed launch ends.
-NCU_TRAFFIC = {"decode": 33832960, "prefill_scan": 101771520}
+NCU_TRAFFIC = {"decode": 33832960, "prefill_scan": 100973312}
 
 
 def env_int(name, default):
