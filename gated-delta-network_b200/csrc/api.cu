@@ -140,6 +140,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     p.status = reinterpret_cast<int*>(ws + lay.off_status);
     p.chunk_base = reinterpret_cast<int*>(ws + lay.off_base);
     p.chunk_seq = reinterpret_cast<int*>(ws + lay.off_seq);
+    p.long_list = reinterpret_cast<int*>(ws + lay.off_long);
     p.w = reinterpret_cast<uint16_t*>(ws + lay.off_w);
     p.u = reinterpret_cast<float*>(ws + lay.off_u);
     p.qp = reinterpret_cast<uint16_t*>(ws + lay.off_qp);

@@ -39,7 +39,10 @@ struct PrefillArgs {
     int H, HV;             // q/k heads and v heads (HV a multiple of H and of 8; 4 and 8 in the reference)
     int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
     int test_withhold;     // GDN_FLAG_TEST_WITHHOLD_CHUNK: the scan skips chunk 1's copies
-    int short_path;        // 1: sequences of 1..kShortLen tokens go to the recurrent short kernel
+    int short_path;        // 1: sequences of 0..kShortLen tokens go to the recurrent short kernel, and
+                           //    the chunked kernels see only the compacted list of the longer ones
+    int rows;              // sequences the scan grid covers (N, or with short_path a bound on the
+                           // number of longer sequences: min(N, T / (kShortLen + 1)), at least 1)
     int no_short;          // GDN_FLAG_NO_SHORT_PATH
     int l2norm;            // GDN_FLAG_QK_L2NORM: normalise q, k per token and head in-kernel
     int small_n;           // 1: N is small enough for each CTA to derive its chunk slots itself
@@ -52,6 +55,7 @@ struct PrefillArgs {
     int* status;           // [1] first error code of a bounded wait that gave up (0 = none)
     int* chunk_base;       // [N+1] first slot of each sequence (prefix sum of its chunk counts)
     int* chunk_seq;        // [S]   sequence owning each slot, -1 for unused slots
+    int* long_list;        // [N+1] short_path: ids of the sequences longer than kShortLen, then their count
     uint16_t* w;           // [8][S*64][128] bf16   w = T diag(beta e^G) K
     float* u;              // [8][S][16][64][8] f32 u = beta v + (T - I) diag(beta) V, column-group major
     uint16_t* qp;          // [8][S*64][128] bf16   Q' = diag(e^G) Q - Aqk w  (output operand)
@@ -62,7 +66,7 @@ struct PrefillArgs {
 // Byte offsets of the workspace regions for N sequences and T tokens.
 struct PrefillLayout {
     int S;
-    size_t off_status, off_base, off_seq, off_w, off_u, off_qp, off_oi, off_g4, total;
+    size_t off_status, off_base, off_seq, off_long, off_w, off_u, off_qp, off_oi, off_g4, total;
 };
 
 int launch_decode(const DecodeArgs& p, int variant, cudaStream_t stream);
@@ -84,6 +88,8 @@ __host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T, int HV 
     o = prefill_up256(o + sizeof(int) * ((size_t)N + 1));
     L.off_seq = o;
     o = prefill_up256(o + sizeof(int) * (size_t)S);
+    L.off_long = o;
+    o = prefill_up256(o + sizeof(int) * ((size_t)N + 1));
     L.off_w = o;
     o = prefill_up256(o + (size_t)HV * rows * 128 * 2);
     L.off_u = o;

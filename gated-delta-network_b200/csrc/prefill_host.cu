@@ -1,5 +1,7 @@
 // prefill_host.cu -- workspace layout, chunk table kernel, TMA tensor maps and the launch
 // sequence of the chunked prefill (table -> prep -> scan), all on the caller's stream.
+#include <algorithm>
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -24,50 +26,58 @@ int prefill_scan_bv(int N, int HV) {
 
 // ---- chunk table ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) gdn_prefill_table_kernel(PrefillArgs p) {
-    __shared__ int s_warp[32];
+    __shared__ long long s_warp[32];
     __shared__ int s_total;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait();
     pdl_trigger();
     if (tid == 0) *p.status = 0;
-    int running = 0;
+    // Chunk slots go to the sequences the chunked kernels process: all of them, or with the
+    // short path only those longer than kShortLen, which are also listed in order in long_list.
+    int running = 0, running_long = 0;
     for (int base = 0; base < p.N; base += 1024) {
         const int i = base + tid;
-        int nc = 0;
+        int nc = 0, lg = 0;
         if (i < p.N) {
             int s, e;
             seq_bounds(p.cu, p.cu64, i, p.T, s, e);
-            nc = (e - s + kChunk - 1) / kChunk;
+            lg = (!p.short_path || e - s > kShortLen) ? 1 : 0;
+            nc = lg ? (e - s + kChunk - 1) / kChunk : 0;
         }
-        int x = nc;
+        // block-wide exclusive prefix sums of nc and lg (packed: nc < 2^20 per sequence here)
+        const long long packed = ((long long)nc << 32) | (long long)lg;
+        long long x = packed;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, x, off);
+            const long long y = __shfl_up_sync(0xffffffffu, x, off);
             if (lane >= off) x += y;
         }
         if (lane == 31) s_warp[warp] = x;
         __syncthreads();
-        int wpre = 0, total = 0;
+        long long wpre = 0, total = 0;
         for (int w = 0; w < 32; ++w) {
-            const int c = s_warp[w];
+            const long long c = s_warp[w];
             if (w < warp) wpre += c;
             total += c;
         }
-        if (i < p.N) p.chunk_base[i] = running + wpre + x - nc;
-        running += total;
+        const long long excl = wpre + x - packed;
+        if (i < p.N) {
+            p.chunk_base[i] = running + (int)(excl >> 32);
+            if (p.short_path && lg) p.long_list[running_long + (int)(excl & 0xffffffffll)] = i;
+        }
+        running += (int)(total >> 32);
+        running_long += (int)(total & 0xffffffffll);
         __syncthreads();
     }
     if (tid == 0) {
         p.chunk_base[p.N] = running;
+        if (p.short_path) p.long_list[p.N] = running_long;
         s_total = running;
     }
     __syncthreads();
     const int total = s_total;
     for (int i = tid; i < p.N; i += 1024) {
-        int s, e;
-        seq_bounds(p.cu, p.cu64, i, p.T, s, e);
-        const int nc = (e - s + kChunk - 1) / kChunk;
-        const int b0 = p.chunk_base[i];
+        const int b0 = p.chunk_base[i], nc = p.chunk_base[i + 1] - b0;
         for (int c = 0; c < nc && b0 + c < p.S; ++c) p.chunk_seq[b0 + c] = i;
     }
     for (int s = total + tid; s < p.S; s += 1024) p.chunk_seq[s] = -1;
@@ -152,7 +162,11 @@ int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
     // short ones off the critical path of the longest sequence, and a separate launch would only
     // add latency.
     p.short_path = (!p.no_short && p.N > kSmallN) ? 1 : 0;
-    if (p.short_path && p.T > 0 && launch_prefill_short(p, stream) != 0) return -1;
+    // Each sequence the chunked kernels see under the short path has more than kShortLen tokens,
+    // so at most T / (kShortLen + 1) of them exist: the scan and prep grids are sized by that
+    // bound instead of N (no CTA launches just to find its sequence is someone else's).
+    p.rows = p.short_path ? (int)std::max(1, std::min(p.N, p.T / (kShortLen + 1))) : p.N;
+    if (p.short_path && launch_prefill_short(p, stream) != 0) return -1;  // also zero-length sequences
     if (!p.small_n && launch_pdl(gdn_prefill_table_kernel, dim3(1), dim3(1024), 0, stream, p) != cudaSuccess)
         return -1;
     if (p.T > 0) {

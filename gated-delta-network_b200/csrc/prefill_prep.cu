@@ -22,6 +22,8 @@
 //     operands Q' = diag(e^G) Q - Aqk w and oi = Aqk u, so the serial scan needs only
 //     o = scale (Q' h + oi) (the Aqk (u - w h) term of chunk_o, fla_kernels.py:758-796).
 //   * Outputs go to the chunk's workspace slot; rows past the chunk end carry zero / finite padding.
+#include <algorithm>
+
 #include "prefill_kernels.cuh"
 #include "sm100.cuh"
 #include "dbg.cuh"
@@ -658,7 +660,9 @@ int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStrea
     if (cudaFuncSetAttribute(gdn_prefill_prep2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
         cudaSuccess)
         return -1;
-    dim3 grid((unsigned)p.S, (unsigned)p.HV);
+    // with the short path only the longer sequences own slots: at most T / 64 + rows of them
+    const int slots = p.short_path ? std::min(p.S, p.T / kChunk + p.rows) : p.S;
+    dim3 grid((unsigned)std::max(slots, 1), (unsigned)p.HV);
     return launch_pdl(gdn_prefill_prep2_kernel, grid, dim3(kThreads), kSmem, stream, p, maps) == cudaSuccess ? 0 : -1;
 }
 

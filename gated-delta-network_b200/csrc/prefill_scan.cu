@@ -87,14 +87,15 @@ __global__ void __launch_bounds__(288, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;
     const int v0 = blockIdx.x * BV;
-    const int n = blockIdx.y / p.HV, hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
+    const int hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
-    int bos, eos;
-    seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
-    const int len = eos - bos;
-    float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
-
+    // CTA rows: the longest sequence first (N <= 32), so the critical path starts in the first
+    // wave; with the short path, the compacted list of the longer sequences.
+    const int row_i = blockIdx.y / p.HV;
+    const bool active = !p.short_path || row_i < p.long_list[p.N];
+    const int n = p.short_path ? (active ? p.long_list[row_i] : 0)
+                               : (p.small_n ? warp_seq_by_rank(p, row_i) : row_i);
     if (blockIdx.x == 0 && blockIdx.y == 0 && p.T > 0) {
         // Tokens outside [cu[0], cu[N]) belong to no sequence: zero output, as the reference
         // zero-initialises the whole output (reference/gdn_prefill_ref.py:49-51).
@@ -108,6 +109,11 @@ __global__ void __launch_bounds__(288, 1)
         for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += C::kThreads)
             o4[idx] = make_uint4(0, 0, 0, 0);
     }
+    if (!active) return;
+    int bos, eos;
+    seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
+    const int len = eos - bos;
+    float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
     if (len <= 0) {  // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62)
         for (int idx = tid; idx < BV * kD; idx += C::kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
         return;
@@ -329,7 +335,7 @@ static int launch_scan_bv(const PrefillArgs& p, const PrefillMaps& maps, cudaStr
     if (cudaFuncSetAttribute(gdn_prefill_scan2_kernel<BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
         cudaSuccess)
         return -1;
-    dim3 grid(kD / BV, p.N * p.HV);
+    dim3 grid(kD / BV, p.rows * p.HV);
     return launch_pdl(gdn_prefill_scan2_kernel<BV>, grid, dim3(C::kThreads), C::kSmem, stream, p, maps) ==
                    cudaSuccess
                ? 0

@@ -68,13 +68,12 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
     const int hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
-    // longest sequence first (N <= 32), as in prefill_scan.cu
-    const int n = p.small_n ? warp_seq_by_rank(p, blockIdx.y / p.HV) : blockIdx.y / p.HV;
-    int bos, eos;
-    seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
-    const int len = eos - bos;
-    float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
-
+    // CTA rows: the longest sequence first (N <= 32); with the short path, the compacted list of
+    // the longer sequences (as in prefill_scan.cu)
+    const int row_i = blockIdx.y / p.HV;
+    const bool active = !p.short_path || row_i < p.long_list[p.N];
+    const int n = p.short_path ? (active ? p.long_list[row_i] : 0)
+                               : (p.small_n ? warp_seq_by_rank(p, row_i) : row_i);
     if (blockIdx.x == 0 && blockIdx.y == 0 && p.T > 0) {
         // Tokens outside [cu[0], cu[N]) belong to no sequence: zero output
         // (reference/gdn_prefill_ref.py:49-51).
@@ -88,6 +87,11 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
         for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += kThreads)
             o4[idx] = make_uint4(0, 0, 0, 0);
     }
+    if (!active) return;
+    int bos, eos;
+    seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
+    const int len = eos - bos;
+    float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
     if (len <= 0) {  // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62)
         for (int idx = tid; idx < BV * kD; idx += kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
         return;
@@ -322,7 +326,7 @@ int launch_prefill_scan_tc(const PrefillArgs& p, const PrefillMaps& maps, cudaSt
     if (cudaFuncSetAttribute(gdn_prefill_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
         cudaSuccess)
         return -1;
-    dim3 grid(kD / BV, p.N * p.HV);
+    dim3 grid(kD / BV, p.rows * p.HV);
     return launch_pdl(gdn_prefill_scan_tc_kernel, grid, dim3(kThreads), kSmem, stream, p, maps) == cudaSuccess ? 0
                                                                                                                  : -1;
 }
