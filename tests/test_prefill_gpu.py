@@ -164,13 +164,17 @@ def test_prefill_strong_decay_extremes():
     _run_and_check(inp)
 
 
-def test_prefill_graph_capture():
-    inp = gi.prefill_inputs([256, 100], seed=29)
+@pytest.mark.parametrize("lens", [[256, 100], [300] * 4 + [64], [6] * 40 + [100, 0]],
+                         ids=["mma_sync_scan", "tcgen05_scan", "short_path_table"])
+def test_prefill_graph_capture(lens):
+    """Every launch sequence (table, short, prep, both scans) captures into a CUDA graph and
+    replays to the eager result: nothing is read back to the host."""
+    inp = gi.prefill_inputs(lens, seed=29)
     q, k, v, st, A_log, a, dt_bias, b, cu, scale = util.prefill_args(inp)
     ro, rs = gdn.prefill.run(q, k, v, st, A_log, a, dt_bias, b, cu, scale)
     out = torch.empty_like(ro)
     ns = torch.empty_like(rs)
-    ws = torch.empty(gdn.prefill.workspace_bytes(2, 356), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(gdn.prefill.workspace_bytes(len(lens), sum(lens)), dtype=torch.uint8, device="cuda")
     from gdn import prefill as pmod
 
     s = torch.cuda.Stream()
