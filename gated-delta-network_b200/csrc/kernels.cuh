@@ -52,7 +52,7 @@ struct PrefillArgs {
     float* new_state;      // [N, 8, 128, 128]
     // workspace (slot-indexed: slot s holds one 64-token chunk of one sequence; rows past the
     // chunk end are zero / finite padding)
-    int* status;           // [1] first error code of a bounded wait that gave up (0 = none)
+    int* status;           // [0] first error code of a bounded wait that gave up (0 = none); [1], [2] scan / prep work counters
     int* chunk_base;       // [N+1] first slot of each sequence (prefix sum of its chunk counts)
     int* chunk_seq;        // [S]   sequence owning each slot, -1 for unused slots
     int* long_list;        // [N+1] short_path: ids of the sequences longer than kShortLen, then their count

@@ -42,12 +42,10 @@ __device__ __forceinline__ void seq_bounds(const void* cu, int cu64, int n, int 
 // chunk_base / chunk_seq once per call.
 constexpr int kSmallN = 32;
 
-// Sequences of at most this many tokens take the recurrent short-sequence kernel whenever it is
-// launched (PrefillArgs::short_path).  Its SIMT cost grows with the length (3 FMAs per state
-// element per token) while a chunk on the tensor-core path costs about the same for 1..64 tokens;
-// measured on B200 the recurrent path wins up to about two dozen tokens (2.3x at 6 tokens,
-// 1.3x at 16) and loses at 60.
-constexpr int kShortLen = 24;
+// Sequences of at most this many tokens take the one-chunk short-sequence kernel whenever it is
+// launched (PrefillArgs::short_path): a single partial chunk done in one CTA per (sequence,
+// v-head), where the chunked path would spend two launches and a workspace round trip on it.
+constexpr int kShortLen = 32;
 
 __device__ __forceinline__ int seq_nchunks(const PrefillArgs& p, int i) {
     int s, e;
@@ -100,5 +98,6 @@ int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStrea
 int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream);
 int launch_prefill_scan_tc(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_short(const PrefillArgs& p, cudaStream_t stream);
+int launch_prefill_short_rec(const PrefillArgs& p, cudaStream_t stream);
 
 }  // namespace gdn

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(288, 1)
         for (int idx = tid; idx < BV * kD; idx += C::kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
         return;
     }
-    if (p.short_path && len <= kShortLen) return;  // the recurrent short kernel owns it
+    if (p.short_path && len <= kShortLen) return;  // a short-sequence kernel owns it
     const int nchunks = (len + kChunk - 1) / kChunk;
     int slot0;
     if (p.small_n) {

@@ -43,7 +43,7 @@ constexpr uint32_t kOffHb = kStages * kStage;        // h, bf16 [128 K rows][64]
 constexpr uint32_t kOffVh = kOffHb + 128 * 128;      // vn hi, bf16 [64 tokens][64], SW128
 constexpr uint32_t kOffVl = kOffVh + 64 * 128;       // vn lo
 constexpr uint32_t kOffOb = kOffVl + 64 * 128;       // output staging, bf16 [64 tokens][64], 16-byte chunks swizzled
-constexpr uint32_t kOffBar = kOffOb + 64 * 128;      // full[2], empty[2], mma_p, mma_u, abort flag, TMEM slot
+constexpr uint32_t kOffBar = kOffOb + 64 * 128;      // full[2], empty[2], mma_p, mma_u, abort flag, TMEM slot, next item
 constexpr uint32_t kSmemUsed = kOffBar + 8 * (2 * kStages + 2) + 16;
 constexpr uint32_t kSmem = kSmemUsed + 1024;
 constexpr uint32_t kTmemCols = 128;                  // P: columns 0-63, D: 64-127
@@ -64,17 +64,9 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_u + 1) + 1;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int v0 = blockIdx.x * BV;
-    const int hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
-    // CTA rows: the longest sequence first (N <= 32); with the short path, the compacted list of
-    // the longer sequences (as in prefill_scan.cu)
-    const int row_i = blockIdx.y / p.HV;
-    const bool active = !p.short_path || row_i < p.long_list[p.N];
-    const int n = p.short_path ? (active ? p.long_list[row_i] : 0)
-                               : (p.small_n ? warp_seq_by_rank(p, row_i) : row_i);
-    if (blockIdx.x == 0 && blockIdx.y == 0 && p.T > 0) {
+    if (blockIdx.x == 0 && p.T > 0) {
         // Tokens outside [cu[0], cu[N]) belong to no sequence: zero output
         // (reference/gdn_prefill_ref.py:49-51).
         int lo, tmp, hi;
@@ -87,24 +79,15 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
         for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += kThreads)
             o4[idx] = make_uint4(0, 0, 0, 0);
     }
-    if (!active) return;
-    int bos, eos;
-    seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
-    const int len = eos - bos;
-    float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
-    if (len <= 0) {  // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62)
-        for (int idx = tid; idx < BV * kD; idx += kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
-        return;
-    }
-    if (p.short_path && len <= kShortLen) return;  // the recurrent short kernel owns it
-    const int nchunks = (len + kChunk - 1) / kChunk;
-    int slot0;
-    if (p.small_n) {
-        int dummy;
-        warp_chunk_lookup(p, n, -1, &slot0, &dummy);
-    } else {
-        slot0 = p.chunk_base[n];
-    }
+    // Work items: item = (row_i * HV + hv) * 2 + column half.  CTA rows are the longest sequence
+    // first (N <= 32), or with the short path the compacted list of the longer sequences (as in
+    // prefill_scan.cu).  Without the short path the grid holds one CTA per item; with it, the
+    // number of rows is known only on the device, so a grid of at most one CTA per SM takes
+    // items from a counter (status word 1, zeroed by the chunk-table kernel) until they run out,
+    // instead of launching CTAs that would only find their row empty.
+    const bool persistent = p.short_path != 0;
+    const int rows_valid = p.short_path ? p.long_list[p.N] : p.rows;
+    int* item_slot = reinterpret_cast<int*>(tslot + 1);
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -122,199 +105,238 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    if (warp == kMath / 32) {
-        // Producer: refill stage c % 2 with chunk c once the math warps released chunk c - 2.
-        if (lane == 0) {
-            tma_prefetch_desc(&maps.w);
-            tma_prefetch_desc(&maps.qp);
-            tma_prefetch_desc(&maps.k);
-            for (int c = 0; c < nchunks; ++c) {
-                if (c >= kStages && !mbar_wait(empty + (c % kStages), (uint32_t)((c / kStages - 1) & 1), p.status,
-                                               kErrScanTmaTimeout))
-                    break;
-                if (p.test_withhold && c == 1) continue;  // test hook: this chunk's copies never arrive
-                unsigned char* st = sm + (c % kStages) * kStage;
-                uint64_t* bar = full + (c % kStages);
-                const int slot = slot0 + c, wr = slot * kChunk, t0 = bos + c * kChunk;
-                mbar_arrive_expect_tx(bar, kTxBytes);
-                tma_load_3d(st + kOffWQ, &maps.w, 0, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 8192, &maps.qp, 0, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 16384, &maps.w, 64, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 24576, &maps.qp, 64, wr, hv, bar);
-                tma_load_3d(st + kOffK, &maps.k, 0, hq, t0, bar);
-                tma_load_3d(st + kOffK + 8192, &maps.k, 64, hq, t0, bar);
-                bulk_load(st + kOffU, p.u + cg_off(hv, p.S, slot, v0 / 8), 64 * BV * 4, bar);
-                bulk_load(st + kOffO, p.oi + cg_off(hv, p.S, slot, v0 / 8), 64 * BV * 2, bar);
-                bulk_load(st + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, bar);
+    uint32_t cbase = 0;  // chunks this CTA has run through the ring so far
+    int item = blockIdx.x;
+    for (;;) {
+        const int row_i = (item >> 1) / p.HV;
+        if (row_i >= rows_valid) break;  // uniform across the CTA
+        const int v0 = (item & 1) * BV;
+        const int hv = (item >> 1) % p.HV, hq = hv / (p.HV / p.H);
+        const int n = p.short_path ? p.long_list[row_i] : (p.small_n ? warp_seq_by_rank(p, row_i) : row_i);
+        int bos, eos;
+        seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
+        const int len = eos - bos;
+        float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
+        // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62);
+        // with the short path a short-sequence kernel owns the sequences of up to kShortLen tokens
+        const int nchunks = (len <= 0 || (p.short_path && len <= kShortLen)) ? 0 : (len + kChunk - 1) / kChunk;
+        if (len <= 0)
+            for (int idx = tid; idx < BV * kD; idx += kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
+        int slot0 = 0;
+        if (nchunks > 0) {
+            if (p.small_n) {
+                int dummy;
+                warp_chunk_lookup(p, n, -1, &slot0, &dummy);
+            } else {
+                slot0 = p.chunk_base[n];
             }
         }
-    } else {
-        // ---- math warps: thread (r, half) = TMEM lane r, columns 32 half .. 32 half + 31 ----
-        // Warps w and w + 4 share TMEM lane quarter w (lanes 32 w .. 32 w + 31) and split its
-        // 64 columns, so every per-element epilogue is spread over eight warps.
-        const int r = lane + 32 * (warp & 3), half = warp >> 2;
-        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 32u * half;
-        float h[32];  // state row r (K index), columns v0 + 32 half + j
-        {
-            const float* st_in = p.state ? p.state + ((size_t)n * p.HV + hv) * kD * kD : nullptr;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) h[j] = st_in ? st_in[(size_t)(v0 + 32 * half + j) * kD + r] : 0.f;
-        }
-        // bf16 copy of h into the MN-major SW128 operand: 128-byte rows, 16-byte chunks
-        // XOR-swizzled by row % 8; this thread owns chunks 4 half .. 4 half + 3 of row r
-        auto write_hb = [&]() {
-            unsigned char* row = sm + kOffHb + r * 128;
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int j = 4 * half + jj;
-                *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) =
-                    make_uint4(pack_bf16x2(h[8 * jj], h[8 * jj + 1]), pack_bf16x2(h[8 * jj + 2], h[8 * jj + 3]),
-                               pack_bf16x2(h[8 * jj + 4], h[8 * jj + 5]), pack_bf16x2(h[8 * jj + 6], h[8 * jj + 7]));
-            }
-        };
-        write_hb();
-        const bool dbg = blockIdx.x == 0 && blockIdx.y == 0;
-        long long tp = clock64();
-        (void)dbg;
-        constexpr uint32_t idesc_p = umma_idesc_bf16(128, BV, false, true);
-        constexpr uint32_t idesc_u = umma_idesc_bf16(128, BV, true, true);
-        int c = 0;
-        for (; c < nchunks; ++c) {
-            if (!mbar_wait(full + (c % kStages), (uint32_t)((c / kStages) & 1), p.status, kErrScanTmaTimeout))
-                *abort_flag = 1;
-            fence_async_smem();  // this thread's h copy (generic stores) -> the tensor core
-            tc_fence_before();
-            named_bar_sync(1, kMath);
-            if (*abort_flag) break;  // written only before this barrier
-            tc_fence_after();
-            GDN_PH_ACC(dbg, 20, tp);
-            const unsigned char* st = sm + (c % kStages) * kStage;
-            const uint32_t sst = sbase + (uint32_t)(c % kStages) * kStage;
-            const float* G4 = reinterpret_cast<const float*>(st + kOffG);
-            const int t0 = bos + c * kChunk;
-            const int L = min(kChunk, eos - t0);
-            const float GL = G4[(L - 1) * 4];
-            // MMA_P: [W; Q'] x h
-            if (tid == 0) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_bf16(tmem, umma_desc_sw128(sst + kOffWQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
-                              umma_desc_sw128(sbase + kOffHb + 2048u * kk, 8192, 1024), idesc_p, kk > 0);
-                umma_commit(bar_p);
-            }
-            bool ok = mbar_wait(bar_p, (uint32_t)(c & 1), p.status, kErrPrepMmaTimeout);
-            tc_fence_after();
-            GDN_PH_ACC(dbg, 21, tp);
-            {
-                uint32_t d[32];
-                tmem_ld32_async(tl, d);
-                tmem_ld_wait();
-                tmem_regs_ready(d);
-                GDN_PH_ACC(dbg, 25, tp);
-                if (r < 64) {
-                    // vn = (u - w h) e^{G_L - G_r} / |k_r|  -> bf16 hi + lo (MN-major SW128, token row r)
-                    const float ed = __expf(GL - G4[r * 4]) * G4[r * 4 + 3];
-                    const float* Us = reinterpret_cast<const float*>(st + kOffU);
-                    unsigned char* rh = sm + kOffVh + r * 128;
-                    unsigned char* rl = sm + kOffVl + r * 128;
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const int j = 4 * half + jj;
-                        const float4 ua = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8);
-                        const float4 ub = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8 + 4);
-                        const float uu[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
-                        uint32_t hi[4], lo[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float x0 = (uu[2 * e] - __uint_as_float(d[8 * jj + 2 * e])) * ed;
-                            const float x1 = (uu[2 * e + 1] - __uint_as_float(d[8 * jj + 2 * e + 1])) * ed;
-                            hi[e] = pack_bf16x2(x0, x1);
-                            lo[e] = pack_bf16x2(x0 - __uint_as_float(hi[e] << 16), x1 - __uint_as_float(hi[e] & 0xffff0000u));
-                        }
-                        *reinterpret_cast<uint4*>(rh + ((j ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4*>(rl + ((j ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                    }
-                    GDN_PH_ACC(dbg, 22, tp);
-                    // warps 0, 1, 4, 5 alone gate MMA_U: the output rows are not on its path
-                    fence_async_smem();  // vn (generic stores) -> the tensor core
-                    tc_fence_before();
-                    const bool okv = named_bar_and(2, 128, ok);
-                    tc_fence_after();
-                    // MMA_U: K^T x (vn_hi + vn_lo), accumulated in TMEM columns 64-127
-                    if (okv && tid == 0) {
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16(tmem + BV, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
-                                      umma_desc_sw128(sbase + kOffVh + 2048u * kk, 8192, 1024), idesc_u, kk > 0);
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16(tmem + BV, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
-                                      umma_desc_sw128(sbase + kOffVl + 2048u * kk, 8192, 1024), idesc_u, true);
-                        umma_commit(bar_u);
-                    }
-                    ok = okv;
-                } else {
-                    // o = scale (Q' h + oi) for token row m = r - 64, while MMA_U runs.  Rows are
-                    // staged in shared memory and then written row-contiguously (a 16-byte store
-                    // per thread, eight threads per 128-byte row): one thread per row writing its
-                    // own 64 bytes would spread every store instruction over 32 rows.
-                    const int m = r - 64;
-                    const uint16_t* Os = reinterpret_cast<const uint16_t*>(st + kOffO);
-                    unsigned char* ob = sm + kOffOb + m * 128;
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const int j = 4 * half + jj;
-                        const uint4 oo = *reinterpret_cast<const uint4*>(Os + (j * 64 + m) * 8);
-                        const uint32_t ow[4] = {oo.x, oo.y, oo.z, oo.w};
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            pk[e] = pack_bf16x2(p.scale * (__uint_as_float(d[8 * jj + 2 * e]) + __uint_as_float(ow[e] << 16)),
-                                                p.scale * (__uint_as_float(d[8 * jj + 2 * e + 1]) + __uint_as_float(ow[e] & 0xffff0000u)));
-                        *reinterpret_cast<uint4*>(ob + ((j ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    }
-                    named_bar_sync(3, 128);  // the four output warps
-                    const int ot = (warp & 1) * 32 + lane + 64 * half;  // 0 .. 127
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int row = 16 * q + (ot >> 3), ch = ot & 7;
-                        if (row < L) {
-                            const uint4 v = *reinterpret_cast<const uint4*>(sm + kOffOb + row * 128 + ((ch ^ (row & 7)) << 4));
-                            *reinterpret_cast<uint4*>(p.out + ((size_t)(t0 + row) * p.HV + hv) * kD + v0 + 8 * ch) = v;
-                        }
+        if (nchunks > 0) {
+            if (warp == kMath / 32) {
+                // Producer: refill stage c % 2 with chunk c once the math warps released chunk c - 2.
+                if (lane == 0) {
+                    tma_prefetch_desc(&maps.w);
+                    tma_prefetch_desc(&maps.qp);
+                    tma_prefetch_desc(&maps.k);
+                    for (int c = 0; c < nchunks; ++c) {
+                        if (cbase + c >= kStages && !mbar_wait(empty + ((cbase + c) % kStages), (uint32_t)(((cbase + c) / kStages - 1) & 1), p.status,
+                                                       kErrScanTmaTimeout))
+                            break;
+                        if (p.test_withhold && c == 1) continue;  // test hook: this chunk's copies never arrive
+                        unsigned char* st = sm + ((cbase + c) % kStages) * kStage;
+                        uint64_t* bar = full + ((cbase + c) % kStages);
+                        const int slot = slot0 + c, wr = slot * kChunk, t0 = bos + c * kChunk;
+                        mbar_arrive_expect_tx(bar, kTxBytes);
+                        tma_load_3d(st + kOffWQ, &maps.w, 0, wr, hv, bar);
+                        tma_load_3d(st + kOffWQ + 8192, &maps.qp, 0, wr, hv, bar);
+                        tma_load_3d(st + kOffWQ + 16384, &maps.w, 64, wr, hv, bar);
+                        tma_load_3d(st + kOffWQ + 24576, &maps.qp, 64, wr, hv, bar);
+                        tma_load_3d(st + kOffK, &maps.k, 0, hq, t0, bar);
+                        tma_load_3d(st + kOffK + 8192, &maps.k, 64, hq, t0, bar);
+                        bulk_load(st + kOffU, p.u + cg_off(hv, p.S, slot, v0 / 8), 64 * BV * 4, bar);
+                        bulk_load(st + kOffO, p.oi + cg_off(hv, p.S, slot, v0 / 8), 64 * BV * 2, bar);
+                        bulk_load(st + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, bar);
                     }
                 }
-            }
-            // an MMA_U that was not issued (a wait gave up) also fails this bounded wait
-            if (ok) ok = mbar_wait(bar_u, (uint32_t)(c & 1), p.status, kErrPrepMmaTimeout);
-            tc_fence_after();
-            GDN_PH_ACC(dbg, 23, tp);
-            {
-                uint32_t d[32];
-                tmem_ld32_async(tl + BV, d);
-                tmem_ld_wait();
-                tmem_regs_ready(d);
-                const float eL = __expf(GL);
+            } else {
+                // ---- math warps: thread (r, half) = TMEM lane r, columns 32 half .. 32 half + 31 ----
+                // Warps w and w + 4 share TMEM lane quarter w (lanes 32 w .. 32 w + 31) and split its
+                // 64 columns, so every per-element epilogue is spread over eight warps.
+                const int r = lane + 32 * (warp & 3), half = warp >> 2;
+                const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 32u * half;
+                float h[32];  // state row r (K index), columns v0 + 32 half + j
+                {
+                    const float* st_in = p.state ? p.state + ((size_t)n * p.HV + hv) * kD * kD : nullptr;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) h[j] = fmaf(eL, h[j], __uint_as_float(d[j]));
-            }
-            // the stage's smem operands and TMEM results are consumed: hand the stage back
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty + (c % kStages));
-            if (!ok) *abort_flag = 1;
-            write_hb();
-            GDN_PH_ACC(dbg, 24, tp);
-        }
-        if (c < nchunks) {
-            // gave up: let copies already in flight land (bounded) before the CTA exits
-            if (tid == 0)
-                for (int cc = c + 1; cc < min(nchunks, c + kStages); ++cc)
-                    mbar_wait(full + (cc % kStages), (uint32_t)((cc / kStages) & 1), nullptr, 0);
-        } else {
-            // final state (k-last): new_state[n][hv][v0 + 32 half + j][r]
+                    for (int j = 0; j < 32; ++j) h[j] = st_in ? st_in[(size_t)(v0 + 32 * half + j) * kD + r] : 0.f;
+                }
+                // bf16 copy of h into the MN-major SW128 operand: 128-byte rows, 16-byte chunks
+                // XOR-swizzled by row % 8; this thread owns chunks 4 half .. 4 half + 3 of row r
+                auto write_hb = [&]() {
+                    unsigned char* row = sm + kOffHb + r * 128;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) st_out[(size_t)(v0 + 32 * half + j) * kD + r] = h[j];
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const int j = 4 * half + jj;
+                        *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) =
+                            make_uint4(pack_bf16x2(h[8 * jj], h[8 * jj + 1]), pack_bf16x2(h[8 * jj + 2], h[8 * jj + 3]),
+                                       pack_bf16x2(h[8 * jj + 4], h[8 * jj + 5]), pack_bf16x2(h[8 * jj + 6], h[8 * jj + 7]));
+                    }
+                };
+                write_hb();
+                const bool dbg = blockIdx.x == 0;
+                long long tp = clock64();
+                (void)dbg;
+                constexpr uint32_t idesc_p = umma_idesc_bf16(128, BV, false, true);
+                constexpr uint32_t idesc_u = umma_idesc_bf16(128, BV, true, true);
+                int c = 0;
+                for (; c < nchunks; ++c) {
+                    const uint32_t g = cbase + c;  // running chunk count of the CTA: ring stage and barrier phases
+                    if (!mbar_wait(full + (g % kStages), (uint32_t)((g / kStages) & 1), p.status, kErrScanTmaTimeout))
+                        *abort_flag = 1;
+                    fence_async_smem();  // this thread's h copy (generic stores) -> the tensor core
+                    tc_fence_before();
+                    named_bar_sync(1, kMath);
+                    if (*abort_flag) break;  // written only before this barrier
+                    tc_fence_after();
+                    GDN_PH_ACC(dbg, 20, tp);
+                    const unsigned char* st = sm + (g % kStages) * kStage;
+                    const uint32_t sst = sbase + (uint32_t)(g % kStages) * kStage;
+                    const float* G4 = reinterpret_cast<const float*>(st + kOffG);
+                    const int t0 = bos + c * kChunk;
+                    const int L = min(kChunk, eos - t0);
+                    const float GL = G4[(L - 1) * 4];
+                    // MMA_P: [W; Q'] x h
+                    if (tid == 0) {
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk)
+                            umma_bf16(tmem, umma_desc_sw128(sst + kOffWQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+                                      umma_desc_sw128(sbase + kOffHb + 2048u * kk, 8192, 1024), idesc_p, kk > 0);
+                        umma_commit(bar_p);
+                    }
+                    bool ok = mbar_wait(bar_p, g & 1u, p.status, kErrPrepMmaTimeout);
+                    tc_fence_after();
+                    GDN_PH_ACC(dbg, 21, tp);
+                    {
+                        uint32_t d[32];
+                        tmem_ld32_async(tl, d);
+                        tmem_ld_wait();
+                        tmem_regs_ready(d);
+                        GDN_PH_ACC(dbg, 25, tp);
+                        if (r < 64) {
+                            // vn = (u - w h) e^{G_L - G_r} / |k_r|  -> bf16 hi + lo (MN-major SW128, token row r)
+                            const float ed = __expf(GL - G4[r * 4]) * G4[r * 4 + 3];
+                            const float* Us = reinterpret_cast<const float*>(st + kOffU);
+                            unsigned char* rh = sm + kOffVh + r * 128;
+                            unsigned char* rl = sm + kOffVl + r * 128;
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj) {
+                                const int j = 4 * half + jj;
+                                const float4 ua = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8);
+                                const float4 ub = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8 + 4);
+                                const float uu[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+                                uint32_t hi[4], lo[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float x0 = (uu[2 * e] - __uint_as_float(d[8 * jj + 2 * e])) * ed;
+                                    const float x1 = (uu[2 * e + 1] - __uint_as_float(d[8 * jj + 2 * e + 1])) * ed;
+                                    hi[e] = pack_bf16x2(x0, x1);
+                                    lo[e] = pack_bf16x2(x0 - __uint_as_float(hi[e] << 16), x1 - __uint_as_float(hi[e] & 0xffff0000u));
+                                }
+                                *reinterpret_cast<uint4*>(rh + ((j ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                                *reinterpret_cast<uint4*>(rl + ((j ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            }
+                            GDN_PH_ACC(dbg, 22, tp);
+                            // warps 0, 1, 4, 5 alone gate MMA_U: the output rows are not on its path
+                            fence_async_smem();  // vn (generic stores) -> the tensor core
+                            tc_fence_before();
+                            const bool okv = named_bar_and(2, 128, ok);
+                            tc_fence_after();
+                            // MMA_U: K^T x (vn_hi + vn_lo), accumulated in TMEM columns 64-127
+                            if (okv && tid == 0) {
+#pragma unroll
+                                for (int kk = 0; kk < 4; ++kk)
+                                    umma_bf16(tmem + BV, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
+                                              umma_desc_sw128(sbase + kOffVh + 2048u * kk, 8192, 1024), idesc_u, kk > 0);
+#pragma unroll
+                                for (int kk = 0; kk < 4; ++kk)
+                                    umma_bf16(tmem + BV, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
+                                              umma_desc_sw128(sbase + kOffVl + 2048u * kk, 8192, 1024), idesc_u, true);
+                                umma_commit(bar_u);
+                            }
+                            ok = okv;
+                        } else {
+                            // o = scale (Q' h + oi) for token row m = r - 64, while MMA_U runs.  Rows are
+                            // staged in shared memory and then written row-contiguously (a 16-byte store
+                            // per thread, eight threads per 128-byte row): one thread per row writing its
+                            // own 64 bytes would spread every store instruction over 32 rows.
+                            const int m = r - 64;
+                            const uint16_t* Os = reinterpret_cast<const uint16_t*>(st + kOffO);
+                            unsigned char* ob = sm + kOffOb + m * 128;
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj) {
+                                const int j = 4 * half + jj;
+                                const uint4 oo = *reinterpret_cast<const uint4*>(Os + (j * 64 + m) * 8);
+                                const uint32_t ow[4] = {oo.x, oo.y, oo.z, oo.w};
+                                uint32_t pk[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e)
+                                    pk[e] = pack_bf16x2(p.scale * (__uint_as_float(d[8 * jj + 2 * e]) + __uint_as_float(ow[e] << 16)),
+                                                        p.scale * (__uint_as_float(d[8 * jj + 2 * e + 1]) + __uint_as_float(ow[e] & 0xffff0000u)));
+                                *reinterpret_cast<uint4*>(ob + ((j ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            }
+                            named_bar_sync(3, 128);  // the four output warps
+                            const int ot = (warp & 1) * 32 + lane + 64 * half;  // 0 .. 127
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const int row = 16 * q + (ot >> 3), ch = ot & 7;
+                                if (row < L) {
+                                    const uint4 v = *reinterpret_cast<const uint4*>(sm + kOffOb + row * 128 + ((ch ^ (row & 7)) << 4));
+                                    *reinterpret_cast<uint4*>(p.out + ((size_t)(t0 + row) * p.HV + hv) * kD + v0 + 8 * ch) = v;
+                                }
+                            }
+                        }
+                    }
+                    // an MMA_U that was not issued (a wait gave up) also fails this bounded wait
+                    if (ok) ok = mbar_wait(bar_u, g & 1u, p.status, kErrPrepMmaTimeout);
+                    tc_fence_after();
+                    GDN_PH_ACC(dbg, 23, tp);
+                    {
+                        uint32_t d[32];
+                        tmem_ld32_async(tl + BV, d);
+                        tmem_ld_wait();
+                        tmem_regs_ready(d);
+                        const float eL = __expf(GL);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) h[j] = fmaf(eL, h[j], __uint_as_float(d[j]));
+                    }
+                    // the stage's smem operands and TMEM results are consumed: hand the stage back
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty + (g % kStages));
+                    if (!ok) *abort_flag = 1;
+                    write_hb();
+                    GDN_PH_ACC(dbg, 24, tp);
+                }
+                if (c < nchunks) {
+                    // gave up: let copies already in flight land (bounded) before the CTA exits
+                    if (tid == 0)
+                        for (int cc = c + 1; cc < min(nchunks, c + kStages); ++cc)
+                            mbar_wait(full + ((cbase + cc) % kStages), (uint32_t)(((cbase + cc) / kStages) & 1), nullptr, 0);
+                } else {
+                    // final state (k-last): new_state[n][hv][v0 + 32 half + j][r]
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) st_out[(size_t)(v0 + 32 * half + j) * kD + r] = h[j];
+                }
+            }
         }
+        cbase += (uint32_t)nchunks;
+        // next item: every warp is done with this one (operands, TMEM, the h copy)
+        tc_fence_before();
+        __syncthreads();
+        if (*abort_flag || !persistent) break;
+        if (tid == 0) *item_slot = (int)gridDim.x + atomicAdd(p.status + 1, 1);
+        __syncthreads();
+        tc_fence_after();
+        item = *item_slot;
     }
     tc_fence_before();
     __syncthreads();
@@ -326,7 +348,16 @@ int launch_prefill_scan_tc(const PrefillArgs& p, const PrefillMaps& maps, cudaSt
     if (cudaFuncSetAttribute(gdn_prefill_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
         cudaSuccess)
         return -1;
-    dim3 grid(kD / BV, p.rows * p.HV);
+    const long long items = (long long)p.rows * p.HV * (kD / BV);
+    long long ctas = items;
+    if (p.short_path) {  // at most one CTA per SM, taking items from the counter
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return -1;
+        ctas = std::min<long long>(items, sms);
+    }
+    dim3 grid((unsigned)std::max<long long>(ctas, 1));
     return launch_pdl(gdn_prefill_scan_tc_kernel, grid, dim3(kThreads), kSmem, stream, p, maps) == cudaSuccess ? 0
                                                                                                                  : -1;
 }

@@ -1,0 +1,161 @@
+// prefill_short_rec.cu -- token-recurrent path for batches of very short prefill sequences.
+//
+// The short-sequence kernel of prefill_short.cu spends one CTA per (sequence, v-head) on a padded
+// 32-token chunk; for sequences of a handful of tokens the plain recurrence is cheaper.  This
+// kernel keeps a slice of the state in registers and applies the token-sequential recurrence of
+// reference/gdn_prefill_ref.py:71-87
+// directly (the fused form of the decode step, csrc/decode.cu), one token after another, so each
+// state byte is read and written once and the arithmetic stays fp32 throughout.  Sequences longer
+// than kShortLen are left to the chunked kernels, which then see only those (PrefillArgs::
+// short_path, long_list); zero-length sequences (all-zero final state) are handled here too.
+//
+// Mapping: CTA = (32-row slice of the k-last state, sequence n, v-head hv), 128 threads; 8 lanes
+// share a pair of state rows (r and r + 16 of the slice), lane j holding K elements
+// {32 i + 4 j .. +3 : i = 0..3} of both.  A parallel staging phase converts the sequence's q and k
+// (its q/k head) to fp32 in shared memory once -- normalised there when the in-kernel L2 norm is
+// on -- together with q.k, the gates and this slice's v, so the per-token loop is only
+//   sk = S.k, sq = S.q (one 3-step butterfly for both rows), vn = beta (v - g sk),
+//   out = scale (g sq + vn (q.k)), S = g S + vn k,
+// with every q / k load shared by two state rows.
+#include "prefill_kernels.cuh"
+
+namespace gdn {
+
+constexpr int kRecRows = 32;                   // state rows (V) per CTA
+constexpr int kRecThreads = kRecRows * 4;      // 8 lanes per row pair
+
+__global__ void __launch_bounds__(kRecThreads) gdn_prefill_short_rec_kernel(PrefillArgs p) {
+    __shared__ __align__(16) float sq_[kShortLen][kD];  // q (normalised with the L2 norm), fp32
+    __shared__ __align__(16) float sk_[kShortLen][kD];  // k, likewise
+    __shared__ __align__(16) uint16_t sv_[kShortLen][kRecRows];
+    __shared__ float sg_[kShortLen], sb_[kShortLen], skq_[kShortLen];
+
+    const int n = blockIdx.y / p.HV, hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
+    pdl_wait();
+    pdl_trigger();
+    int bos, eos;
+    seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
+    const int len = eos - bos;
+    if (len > kShortLen) return;  // the chunked kernels own these sequences
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7;
+    const int r0 = blockIdx.x * kRecRows;
+    const int rowa = r0 + (tid >> 3), rowb = rowa + kRecRows / 2;  // state rows (V index)
+    const size_t sbase = ((size_t)n * p.HV + hv) * kD * kD + 4 * j;
+    const size_t offa = sbase + (size_t)rowa * kD, offb = sbase + (size_t)rowb * kD;
+
+    float4 Sa[4], Sb[4];
+    if (len <= 0) {  // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            st_stream_f4(p.new_state + offa + 32 * i, make_float4(0.f, 0.f, 0.f, 0.f));
+            st_stream_f4(p.new_state + offb + 32 * i, make_float4(0.f, 0.f, 0.f, 0.f));
+        }
+        return;
+    }
+    if (p.state) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            Sa[i] = ld_stream_f4(p.state + offa + 32 * i);
+            Sb[i] = ld_stream_f4(p.state + offb + 32 * i);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) Sa[i] = Sb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // ---- staging: warp w takes tokens w, w + 4, ...; lane l converts elements 4 l .. 4 l + 3 ----
+    for (int t = warp; t < len; t += kRecThreads / 32) {
+        const size_t g = ((size_t)(bos + t) * p.H + hq) * kD + 4 * lane;
+        const uint2 qq = *reinterpret_cast<const uint2*>(p.q + g);
+        const uint2 kk = *reinterpret_cast<const uint2*>(p.k + g);
+        float4 q4 = make_float4(__uint_as_float(qq.x << 16), __uint_as_float(qq.x & 0xffff0000u),
+                                __uint_as_float(qq.y << 16), __uint_as_float(qq.y & 0xffff0000u));
+        float4 k4 = make_float4(__uint_as_float(kk.x << 16), __uint_as_float(kk.x & 0xffff0000u),
+                                __uint_as_float(kk.y << 16), __uint_as_float(kk.y & 0xffff0000u));
+        if (p.l2norm) {  // x / sqrt(sum x^2 + 1e-6) per token and head
+            float ssq = q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w;
+            float ssk = k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                ssq += __shfl_xor_sync(0xffffffffu, ssq, off);
+                ssk += __shfl_xor_sync(0xffffffffu, ssk, off);
+            }
+            const float rq = rsqrtf(ssq + 1e-6f), rk = rsqrtf(ssk + 1e-6f);
+            q4 = make_float4(q4.x * rq, q4.y * rq, q4.z * rq, q4.w * rq);
+            k4 = make_float4(k4.x * rk, k4.y * rk, k4.z * rk, k4.w * rk);
+        }
+        *reinterpret_cast<float4*>(&sq_[t][4 * lane]) = q4;
+        *reinterpret_cast<float4*>(&sk_[t][4 * lane]) = k4;
+        float kq = q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) kq += __shfl_xor_sync(0xffffffffu, kq, off);
+        if (lane == 0) {
+            const size_t gg = (size_t)(bos + t) * p.HV + hv;
+            skq_[t] = kq;
+            sg_[t] = expf(log_decay(bf2f(p.a[gg]), p.A_log[hv], p.dt_bias[hv]));
+            sb_[t] = sigmoidf_(bf2f(p.b[gg]));
+        }
+    }
+    for (int idx = tid; idx < len * (kRecRows / 8); idx += kRecThreads) {
+        const int t = idx / (kRecRows / 8), c = idx % (kRecRows / 8);
+        *reinterpret_cast<uint4*>(&sv_[t][8 * c]) =
+            *reinterpret_cast<const uint4*>(p.v + ((size_t)(bos + t) * p.HV + hv) * kD + r0 + 8 * c);
+    }
+    __syncthreads();
+
+    const int ra = tid >> 3, rb = ra + kRecRows / 2;  // rows within the slice
+    for (int t = 0; t < len; ++t) {
+        float4 qv[4], kv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            qv[i] = *reinterpret_cast<const float4*>(&sq_[t][32 * i + 4 * j]);
+            kv[i] = *reinterpret_cast<const float4*>(&sk_[t][32 * i + 4 * j]);
+        }
+        const float g = sg_[t], beta = sb_[t], kq = skq_[t];
+        float ska = 0.f, sqa = 0.f, skb = 0.f, sqb = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            ska = fmaf(Sa[i].x, kv[i].x, fmaf(Sa[i].y, kv[i].y, fmaf(Sa[i].z, kv[i].z, fmaf(Sa[i].w, kv[i].w, ska))));
+            sqa = fmaf(Sa[i].x, qv[i].x, fmaf(Sa[i].y, qv[i].y, fmaf(Sa[i].z, qv[i].z, fmaf(Sa[i].w, qv[i].w, sqa))));
+            skb = fmaf(Sb[i].x, kv[i].x, fmaf(Sb[i].y, kv[i].y, fmaf(Sb[i].z, kv[i].z, fmaf(Sb[i].w, kv[i].w, skb))));
+            sqb = fmaf(Sb[i].x, qv[i].x, fmaf(Sb[i].y, qv[i].y, fmaf(Sb[i].z, qv[i].z, fmaf(Sb[i].w, qv[i].w, sqb))));
+        }
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) {
+            ska += __shfl_xor_sync(0xffffffffu, ska, off);
+            sqa += __shfl_xor_sync(0xffffffffu, sqa, off);
+            skb += __shfl_xor_sync(0xffffffffu, skb, off);
+            sqb += __shfl_xor_sync(0xffffffffu, sqb, off);
+        }
+        const float vna = beta * (bf2f(sv_[t][ra]) - g * ska);
+        const float vnb = beta * (bf2f(sv_[t][rb]) - g * skb);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            Sa[i].x = fmaf(g, Sa[i].x, vna * kv[i].x);
+            Sa[i].y = fmaf(g, Sa[i].y, vna * kv[i].y);
+            Sa[i].z = fmaf(g, Sa[i].z, vna * kv[i].z);
+            Sa[i].w = fmaf(g, Sa[i].w, vna * kv[i].w);
+            Sb[i].x = fmaf(g, Sb[i].x, vnb * kv[i].x);
+            Sb[i].y = fmaf(g, Sb[i].y, vnb * kv[i].y);
+            Sb[i].z = fmaf(g, Sb[i].z, vnb * kv[i].z);
+            Sb[i].w = fmaf(g, Sb[i].w, vnb * kv[i].w);
+        }
+        if (j == 0) {
+            uint16_t* o = p.out + ((size_t)(bos + t) * p.HV + hv) * kD;
+            o[rowa] = f2bf(p.scale * (g * sqa + vna * kq));
+            o[rowb] = f2bf(p.scale * (g * sqb + vnb * kq));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        st_stream_f4(p.new_state + offa + 32 * i, Sa[i]);
+        st_stream_f4(p.new_state + offb + 32 * i, Sb[i]);
+    }
+}
+
+int launch_prefill_short_rec(const PrefillArgs& p, cudaStream_t stream) {
+    dim3 grid(kD / kRecRows, p.N * p.HV);
+    return launch_pdl(gdn_prefill_short_rec_kernel, grid, dim3(kRecThreads), 0, stream, p) == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace gdn

@@ -47,7 +47,7 @@ enum gdn_status {
  * GDN_DEVSTATUS_SCAN_TMA_TIMEOUT in the workspace status word and returns without hanging.
  * Outputs of such a call are invalid.  Never set in production. */
 #define GDN_FLAG_TEST_WITHHOLD_CHUNK 0x1u
-/* Tuning: keep every prefill sequence on the chunked kernels (no recurrent short-sequence path). */
+/* Tuning: keep every prefill sequence on the chunked kernels (no short-sequence path). */
 #define GDN_FLAG_NO_SHORT_PATH 0x2u
 /* Variant for gdn_decode_fwd, gdn_prefill_fwd and gdn_prefill_fwd_noalloc: normalise q and k of every
  * token and q/k head in-kernel, x * (sum x^2 + 1e-6)^-1/2 in fp32, before the step (the in-kernel L2

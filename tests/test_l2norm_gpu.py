@@ -2,7 +2,7 @@
 decode and prefill on raw, un-normalised q / k against the CPU oracle with the same variant
 (x * (sum x^2 + 1e-6)^-1/2 per token and head, tests/bench_decode_sweep.py:43-46), through the
 C ABI.  The prefill cases cover one chunk, ragged multi-chunk sequences, zero-length sequences,
-the recurrent short-sequence path (more than 32 sequences) and both scan slice widths."""
+the short-sequence path (more than 32 sequences) and both scan slice widths."""
 import numpy as np
 import pytest
 import torch
@@ -39,10 +39,10 @@ def test_decode_l2norm_in_place_dps():
     util.check_state(st.cpu().numpy(), rs, rel_l2=1e-5)
 
 
-PREFILL_CASES = [[1], [64], [200], [130, 0, 77, 300], [1024], [6] * 40 + [100, 3, 70]]
+PREFILL_CASES = [[1], [64], [200], [130, 0, 77, 300], [1024], [6] * 40 + [100, 3, 70], [20] * 40 + [100, 3, 70]]
 
 
-@pytest.mark.parametrize("lens", PREFILL_CASES, ids=["1", "64", "200", "mixed4", "1024", "short43"])
+@pytest.mark.parametrize("lens", PREFILL_CASES, ids=["1", "64", "200", "mixed4", "1024", "short43", "short43tc"])
 def test_prefill_l2norm_matches_oracle(lens):
     inp = gi.prefill_inputs(lens, seed=400 + len(lens), normalized=False)
     out, ns = gdn.prefill.run(*util.prefill_args(inp), use_qk_l2norm_in_kernel=True)
