@@ -279,3 +279,51 @@ def test_prefill_short_sequence_path(lens):
     torch.cuda.synchronize()
     util.check_out(util.bits(o2), util.bits(o1), atol=2e-3, rtol=2e-2)
     util.check_state(s2.cpu().numpy(), s1.cpu().numpy(), rel_l2=1e-4)
+
+
+def test_prefill_persistent_grids_many_items():
+    """With the short path on (more than 32 sequences), the prep and tcgen05-scan kernels run
+    persistent grids of at most one or two CTAs per SM that take work items from device counters.
+    160 sequences of 33-300 tokens plus short ones give ~2,500 scan items and ~2,800 prep items,
+    so every CTA runs many items back to back (mbarrier phases carried across items).  The result
+    must match the oracle and the one-CTA-per-item route (GDN_FLAG_NO_SHORT_PATH)."""
+    from gdn import prefill as pmod
+
+    rng = np.random.default_rng(41)
+    lens = rng.integers(33, 301, 160).tolist() + [0, 5, 32, 1] * 5
+    rng.shuffle(lens)
+    inp = gi.prefill_inputs(lens, seed=41)
+    _run_and_check(inp)
+    args = util.prefill_args(inp)
+    o1, s1 = gdn.prefill.run(*args)
+    o2 = torch.empty_like(o1)
+    s2 = torch.empty_like(s1)
+    pmod._launch(*args, o2, s2, flags=2)  # GDN_FLAG_NO_SHORT_PATH
+    torch.cuda.synchronize()
+    util.check_out(util.bits(o2), util.bits(o1), atol=2e-3, rtol=2e-2)
+    util.check_state(s2.cpu().numpy(), s1.cpu().numpy(), rel_l2=1e-4)
+
+
+@pytest.mark.timeout(120)
+def test_prefill_bounded_wait_persistent_scan():
+    """Failure detection inside the persistent tcgen05 scan: with the test hook every item's
+    second chunk is withheld, the bounded waits expire, each CTA records status 1, leaves its item
+    loop and frees its TMEM; the next call on the same workspace is correct."""
+    from gdn import prefill as pmod
+
+    lens = [100] * 40
+    inp = gi.prefill_inputs(lens, seed=42)
+    args = util.prefill_args(inp)
+    T = sum(lens)
+    out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(len(lens), 8, 128, 128, dtype=torch.float32, device="cuda")
+    ws = torch.empty(gdn.prefill.workspace_bytes(len(lens), T), dtype=torch.uint8, device="cuda")
+    pmod._launch(*args, out, ns, workspace=ws, flags=1 | (64 << 8))  # GDN_FLAG_TEST_WITHHOLD_CHUNK
+    torch.cuda.synchronize()
+    assert gdn.prefill.read_status(ws) == 1  # GDN_DEVSTATUS_SCAN_TMA_TIMEOUT
+    pmod._launch(*args, out, ns, workspace=ws)
+    torch.cuda.synchronize()
+    assert gdn.prefill.read_status(ws) == 0
+    ro, rs = _oracle(inp)
+    util.check_out(util.bits(out), ro)
+    util.check_state(ns.cpu().numpy(), rs)
