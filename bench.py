@@ -9,7 +9,10 @@ Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed
     (8 x 32 MiB = 256 MiB > the 126 MB L2, so every launch streams its state from HBM).
   * prefill_8k: one 8192-token sequence (cu_seqlens = [0, 8192], initial state N(0, 0.02)),
     tokens/s; L2 flushed (256 MiB write) before every timed step, per-step CUDA events.
-  * prefill_configs: one 1024-token sequence, 16 log-uniform varlen sequences (total <= 32768)
+  * decode_sweep (config 1): B = 1 .. 512, each over rotating state buffers (>= 384 MiB), beside
+    the reference's published latencies.
+  * prefill_configs: single sequences of 64 .. 4096 tokens (beside the reference's published table),
+    one 1024-token sequence, 16 log-uniform varlen sequences (total <= 32768)
     and 8 packed 1024-token sequences per GPU, timed the same way; plus 64 x 4096 tokens split by
     sequence over the ranks (strong scaling; whole-job tokens/s over the slowest rank).
   * e2e: the same two metrics through the public API (gdn.decode.kernel / gdn.prefill.kernel)
@@ -317,6 +320,43 @@ def main():
     barrier()
     dec_eager_ms = max_over_ranks(ev0.elapsed_time(ev1) / steps)
 
+    # ---------------- decode batch sweep (config 1), beside the reference's published latencies ----------------
+    def time_decode(bs):
+        sbytes = bs * STATE_BYTES_PER_ELEM
+        nb = max(2, min(768, -(-(384 << 20) // sbytes)))  # rotating state buffers: >= 384 MiB, 3x the L2
+        sq, sk = l2n(randn((bs, 1, H, D))), l2n(randn((bs, 1, H, D)))
+        sv = randn((bs, 1, HV, D), dtype=torch.bfloat16)
+        sa, sb = randn((bs, 1, HV), dtype=torch.bfloat16), randn((bs, 1, HV), dtype=torch.bfloat16)
+        sts = [randn((bs, HV, D, D), 0.02) for _ in range(nb)]
+        so = torch.empty((bs, 1, HV, D), dtype=torch.bfloat16, device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for st in sts:
+                gdn.decode.kernel(sq, sk, sv, st, A_log, sa, dt_bias, sb, scale, so, st)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for st in sts:
+                gdn.decode.kernel(sq, sk, sv, st, A_log, sa, dt_bias, sb, scale, so, st)
+        reps = max(2, 400 // nb)
+        g.replay()
+        barrier()
+        ev0.record()
+        for _ in range(reps):
+            g.replay()
+        ev1.record()
+        barrier()
+        ms = max_over_ranks(ev0.elapsed_time(ev1) / (reps * nb))
+        del g, sts
+        return {"us_per_step": round(ms * 1e3, 3), "state_GBps": round(2 * sbytes / (ms * 1e-3) / 1e9, 1),
+                "frac_of_hbm_peak": round(2 * sbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4)}
+
+    # the reference's published Triton decode latencies on B200 (README.md:42-49, OPTIMIZATION_LOG.md:44, 56-57)
+    ref_decode_us = {1: 26.0, 4: 23.5, 8: 23.5, 16: 23.5, 32: 23.5, 48: 23.5, 64: 23.5, 128: 27.89, 512: 86.79}
+    decode_sweep = {}
+    for bs in (1, 4, 8, 16, 32, 48, 64, 128, 512):
+        decode_sweep[f"B={bs}"] = dict(time_decode(bs), reference_published_us=ref_decode_us[bs])
+
     # ---------------- prefill 8K ----------------
     T = PREFILL_T
     pq = l2n(randn((T, H, D)))
@@ -391,6 +431,12 @@ def main():
 
     prefill_more = {
         "1x1024 (config 2, zero initial state)": time_prefill([1024], False),
+        # single sequences at the lengths of the reference's published prefill table (README.md:86-90, 106-107)
+        "1x64": dict(time_prefill([64], True), reference_published_ms=0.202),
+        "1x256": dict(time_prefill([256], True), reference_published_ms=0.204),
+        "1x512": dict(time_prefill([512], True), reference_published_ms=0.199),
+        "1x2048": dict(time_prefill([2048], True), reference_published_ms=0.229),
+        "1x4096": dict(time_prefill([4096], True), reference_published_ms=0.420),
         "16 varlen, log-uniform [6, 8192] (config 3)": time_prefill(varlen_lengths(), True),
         "8x1024 packed": time_prefill([1024] * 8, True),
         "64x4096 partitioned (config 4)": c4,
@@ -493,6 +539,7 @@ def main():
                    "timing": "CUDA graph replays, CUDA events, max over ranks"},
         "decode_us_per_step": round(dec_us, 3),
         "decode_eager_us_per_step": round(dec_eager_ms * 1e3, 3),
+        "decode_sweep": decode_sweep,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": NCU_TRAFFIC["decode"],
                      "kernel": "gdn_decode_kernel", "peak_source": peak_src},
