@@ -43,6 +43,8 @@ struct PrefillArgs {
                            //    the chunked kernels see only the compacted list of the longer ones
     int rows;              // sequences the scan grid covers (N, or with short_path a bound on the
                            // number of longer sequences: min(N, T / (kShortLen + 1)), at least 1)
+    int only_short;        // 1: T <= kShortLen, so every sequence is short: the short kernel is the only
+                           //    launch and also zeroes unowned output rows and the status word
     int no_short;          // GDN_FLAG_NO_SHORT_PATH
     int l2norm;            // GDN_FLAG_QK_L2NORM: normalise q, k per token and head in-kernel
     int small_n;           // 1: N is small enough for each CTA to derive its chunk slots itself

@@ -164,8 +164,10 @@ int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
     // Short sequences (0..kShortLen tokens) take a dedicated one-launch kernel in batches of many
     // sequences, where its throughput wins; with few sequences the chunked kernels process the
     // short ones off the critical path of the longest sequence, and a separate launch would only
-    // add latency.
-    p.short_path = (!p.no_short && p.N > kSmallN) ? 1 : 0;
+    // add latency.  When T <= kShortLen every sequence is short, so the short kernel is the
+    // call's only launch (no chunk table, prep or scan).
+    p.only_short = (!p.no_short && p.T <= kShortLen) ? 1 : 0;
+    p.short_path = (!p.no_short && (p.N > kSmallN || p.only_short)) ? 1 : 0;
     // Each sequence the chunked kernels see under the short path has more than kShortLen tokens,
     // so at most T / (kShortLen + 1) of them exist: the scan and prep grids are sized by that
     // bound instead of N (no CTA launches just to find its sequence is someone else's).
@@ -177,6 +179,7 @@ int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
     if (p.short_path &&
         ((p.T <= 10 * p.N ? launch_prefill_short_rec(p, stream) : launch_prefill_short(p, stream)) != 0))
         return -1;
+    if (p.only_short) return 0;
     if (!p.small_n && launch_pdl(gdn_prefill_table_kernel, dim3(1), dim3(1024), 0, stream, p) != cudaSuccess)
         return -1;
     if (p.T > 0) {

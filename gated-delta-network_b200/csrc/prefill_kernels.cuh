@@ -47,6 +47,22 @@ constexpr int kSmallN = 32;
 // v-head), where the chunked path would spend two launches and a workspace round trip on it.
 constexpr int kShortLen = 32;
 
+// Tokens outside [cu[0], cu[N]) belong to no sequence: their output rows are zero, as the
+// reference zero-initialises the whole output (reference/gdn_prefill_ref.py:49-51).  One CTA of
+// each call runs this (`tid` of `nthreads`).
+__device__ __forceinline__ void zero_unowned_tokens(const PrefillArgs& p, int tid, int nthreads) {
+    if (p.T <= 0) return;
+    int lo, tmp, hi;
+    seq_bounds(p.cu, p.cu64, 0, p.T, lo, tmp);
+    seq_bounds(p.cu, p.cu64, p.N - 1, p.T, tmp, hi);
+    hi = max(hi, lo);
+    const size_t row_words = (size_t)p.HV * kD / 8;
+    uint4* o4 = reinterpret_cast<uint4*>(p.out);
+    for (size_t idx = tid; idx < (size_t)lo * row_words; idx += nthreads) o4[idx] = make_uint4(0, 0, 0, 0);
+    for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += nthreads)
+        o4[idx] = make_uint4(0, 0, 0, 0);
+}
+
 __device__ __forceinline__ int seq_nchunks(const PrefillArgs& p, int i) {
     int s, e;
     seq_bounds(p.cu, p.cu64, i, p.T, s, e);

@@ -97,17 +97,7 @@ __global__ void __launch_bounds__(288, 1)
     const int n = p.short_path ? (active ? p.long_list[row_i] : 0)
                                : (p.small_n ? warp_seq_by_rank(p, row_i) : row_i);
     if (blockIdx.x == 0 && blockIdx.y == 0 && p.T > 0) {
-        // Tokens outside [cu[0], cu[N]) belong to no sequence: zero output, as the reference
-        // zero-initialises the whole output (reference/gdn_prefill_ref.py:49-51).
-        int lo, tmp, hi;
-        seq_bounds(p.cu, p.cu64, 0, p.T, lo, tmp);
-        seq_bounds(p.cu, p.cu64, p.N - 1, p.T, tmp, hi);
-        hi = max(hi, lo);
-        const size_t row_words = (size_t)p.HV * kD / 8;
-        uint4* o4 = reinterpret_cast<uint4*>(p.out);
-        for (size_t idx = tid; idx < (size_t)lo * row_words; idx += C::kThreads) o4[idx] = make_uint4(0, 0, 0, 0);
-        for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += C::kThreads)
-            o4[idx] = make_uint4(0, 0, 0, 0);
+        zero_unowned_tokens(p, tid, C::kThreads);
     }
     if (!active) return;
     int bos, eos;

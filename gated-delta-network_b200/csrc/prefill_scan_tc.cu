@@ -66,19 +66,7 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
-    if (blockIdx.x == 0 && p.T > 0) {
-        // Tokens outside [cu[0], cu[N]) belong to no sequence: zero output
-        // (reference/gdn_prefill_ref.py:49-51).
-        int lo, tmp, hi;
-        seq_bounds(p.cu, p.cu64, 0, p.T, lo, tmp);
-        seq_bounds(p.cu, p.cu64, p.N - 1, p.T, tmp, hi);
-        hi = max(hi, lo);
-        const size_t row_words = (size_t)p.HV * kD / 8;
-        uint4* o4 = reinterpret_cast<uint4*>(p.out);
-        for (size_t idx = tid; idx < (size_t)lo * row_words; idx += kThreads) o4[idx] = make_uint4(0, 0, 0, 0);
-        for (size_t idx = (size_t)hi * row_words + tid; idx < (size_t)p.T * row_words; idx += kThreads)
-            o4[idx] = make_uint4(0, 0, 0, 0);
-    }
+    if (blockIdx.x == 0) zero_unowned_tokens(p, tid, kThreads);
     // Work items: item = (row_i * HV + hv) * 2 + column half.  CTA rows are the longest sequence
     // first (N <= 32), or with the short path the compacted list of the longer sequences (as in
     // prefill_scan.cu).  Without the short path the grid holds one CTA per item; with it, the

@@ -80,6 +80,10 @@ __global__ void __launch_bounds__(shk::kThreads, 2) gdn_prefill_short_kernel(Pre
     const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();
     pdl_trigger();
+    if (p.only_short && blockIdx.x == 0) {  // the call's only launch
+        if (threadIdx.x == 0) p.status[0] = 0;
+        zero_unowned_tokens(p, threadIdx.x, kThreads);
+    }
     int bos, eos;
     seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
     const int len = eos - bos;

@@ -33,6 +33,10 @@ __global__ void __launch_bounds__(kRecThreads) gdn_prefill_short_rec_kernel(Pref
     const int n = blockIdx.y / p.HV, hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();
     pdl_trigger();
+    if (p.only_short && blockIdx.x == 0 && blockIdx.y == 0) {  // the call's only launch
+        if (threadIdx.x == 0) p.status[0] = 0;
+        zero_unowned_tokens(p, threadIdx.x, kRecThreads);
+    }
     int bos, eos;
     seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
     const int len = eos - bos;

@@ -327,3 +327,36 @@ def test_prefill_bounded_wait_persistent_scan():
     ro, rs = _oracle(inp)
     util.check_out(util.bits(out), ro)
     util.check_state(ns.cpu().numpy(), rs)
+
+
+@pytest.mark.parametrize("lens,cu", [([6], None), ([32], None), ([0, 5, 0, 12], None), ([16, 16], None),
+                                     ([30], [3, 23]), ([9], [2, 7])],
+                         ids=["1x6_rec", "1x32_tc", "4_seqs_rec", "2x16_tc", "unowned_tc", "unowned_rec"])
+def test_prefill_only_short_single_launch(lens, cu):
+    """T <= 32: every sequence is short, so the short-sequence kernel (the token recurrence when
+    T <= 10 N, else the one-chunk tensor-core kernel) is the call's only launch and also zeroes
+    the output rows outside [cu[0], cu[N]) and the status word.  Must match the oracle and the
+    chunked route (GDN_FLAG_NO_SHORT_PATH)."""
+    from gdn import prefill as pmod
+
+    inp = gi.prefill_inputs(lens, seed=43 + sum(lens))
+    if cu is not None:
+        inp["cu_seqlens"] = np.array(cu, np.int32)
+    T = int(sum(lens))
+    args = util.prefill_args(inp)
+    out = torch.full((T, 8, 128), 7.0, dtype=torch.bfloat16, device="cuda")  # stale values must be overwritten
+    ns = torch.empty(len(inp["cu_seqlens"]) - 1, 8, 128, 128, dtype=torch.float32, device="cuda")
+    ws = torch.empty(gdn.prefill.workspace_bytes(ns.shape[0], T), dtype=torch.uint8, device="cuda")
+    ws.fill_(0xFF)  # stale status word
+    pmod._launch(*args, out, ns, workspace=ws)
+    torch.cuda.synchronize()
+    assert gdn.prefill.read_status(ws) == 0
+    ro, rs = _oracle(inp)
+    util.check_out(util.bits(out), ro)
+    util.check_state(ns.cpu().numpy(), rs)
+    o2 = torch.empty_like(out)
+    s2 = torch.empty_like(ns)
+    pmod._launch(*args, o2, s2, flags=2)  # GDN_FLAG_NO_SHORT_PATH
+    torch.cuda.synchronize()
+    util.check_out(util.bits(o2), util.bits(out), atol=2e-3, rtol=2e-2)
+    util.check_state(s2.cpu().numpy(), ns.cpu().numpy(), rel_l2=1e-4)
