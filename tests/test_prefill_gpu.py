@@ -108,8 +108,12 @@ def test_prefill_t1_matches_decode():
     util.check_state(sp.cpu().numpy(), sd.cpu().numpy(), rel_l2=1e-4)
 
 
-def test_prefill_in_place_state_dps():
-    inp = gi.prefill_inputs([90, 200], seed=26)
+@pytest.mark.parametrize("lens", [[90, 200], [1, 24, 25, 3, 200, 0, 17] * 6, [6] * 40, [20], [1000, 7]],
+                         ids=["mma_sync_scan", "short_tc_and_persistent_scan", "short_rec", "only_short", "2seq"])
+def test_prefill_in_place_state_dps(lens):
+    """new_state may be the state tensor itself (in-place write-back) on every route: each CTA
+    reads its slice of the initial state before it writes that slice."""
+    inp = gi.prefill_inputs(lens, seed=26)
     args = util.prefill_args(inp)
     ro, rs = gdn.prefill.run(*args)
     q, k, v, st, A_log, a, dt_bias, b, cu, scale = args
