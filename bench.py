@@ -16,7 +16,8 @@ Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed
     and 8 packed 1024-token sequences per GPU, timed the same way; plus 64 x 4096 tokens split by
     sequence over the ranks (strong scaling; whole-job tokens/s over the slowest rank).
   * e2e: the same two metrics through the public API (gdn.decode.kernel / gdn.prefill.kernel)
-    with pinned host buffers: every step copies its inputs host->device and its results back.
+    with pinned host buffers: every step copies its inputs host->device and its results back,
+    pipelined over copy-in / compute / copy-out streams as a serving loop runs them.
   * cpu_baseline: the CPU oracle (a C restatement of the reference's sequential PyTorch
     loops, all host threads) on a bounded sample of the same workload, rank 0 only.
 --impl reference times that same CPU oracle as the reference arm (the reference itself is
@@ -443,66 +444,88 @@ def main():
     }
 
     # ---------------- e2e through the public API with pinned host buffers ----------------
+    # Every step copies its inputs host -> device from pinned memory, runs the public call and
+    # copies its results back; steps are pipelined as a serving loop would run them: copy-in,
+    # compute and copy-out on three streams over a ring of three device buffer sets, so step i's
+    # device -> host copy overlaps step i + 1's host -> device copy (PCIe is full duplex).  The
+    # timed region runs from the first copy-in to the last copy-out.
+    def pipelined_e2e(h_in, launch, n_steps, n_bufs=3):
+        s_in, s_run, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
+        d_in = [[torch.empty_like(t, device=dev) for t in h_in] for _ in range(n_bufs)]
+        h_out = [None] * n_bufs
+        ev_in = [torch.cuda.Event() for _ in range(n_bufs)]
+        ev_run = [torch.cuda.Event() for _ in range(n_bufs)]
+        ev_out = [torch.cuda.Event() for _ in range(n_bufs)]
+
+        def run(n):
+            for i in range(n):
+                j = i % n_bufs
+                if i >= n_bufs:
+                    s_in.wait_event(ev_out[j])  # buffer set j is free again
+                with torch.cuda.stream(s_in):
+                    for d, h in zip(d_in[j], h_in):
+                        d.copy_(h, non_blocking=True)
+                    ev_in[j].record(s_in)
+                s_run.wait_event(ev_in[j])
+                with torch.cuda.stream(s_run):
+                    outs = launch(j, d_in[j])
+                    ev_run[j].record(s_run)
+                if h_out[j] is None:
+                    h_out[j] = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
+                s_out.wait_event(ev_run[j])
+                with torch.cuda.stream(s_out):
+                    for h, d in zip(h_out[j], outs):
+                        h.copy_(d, non_blocking=True)
+                    ev_out[j].record(s_out)
+
+        cur = torch.cuda.current_stream(dev)
+        for st_ in (s_in, s_run, s_out):
+            st_.wait_stream(cur)
+        run(n_bufs)
+        torch.cuda.synchronize()
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(s_in)
+        run(n_steps)
+        t1.record(s_out)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(t0.elapsed_time(t1) / n_steps)
+
     e2e = None
     pre_e2e = None
     if not args.no_e2e:
-        hq_, hk_, hv_, ha_, hb_ = (t.cpu().pin_memory() for t in (q, k, v, a, b))
-        hst = states[0].cpu().pin_memory()
-        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        hns = torch.empty(hst.shape, dtype=torch.float32).pin_memory()
-        d_in = [torch.empty_like(t, device=dev) for t in (hq_, hk_, hv_, ha_, hb_, hst)]
-        h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, ha_, hb_, hst))
-        d2h = hout.numel() * hout.element_size() + hns.numel() * 4
-        n_e2e = max(3, min(20, args.steps // 10))
+        n_e2e = max(6, min(30, args.steps // 8))
+        h_dec = [t.cpu().pin_memory() for t in (q, k, v, a, b, states[0])]
+        dec_out = [torch.empty_like(out) for _ in range(3)]
 
-        def e2e_step():
-            for dst, src in zip(d_in, (hq_, hk_, hv_, ha_, hb_, hst)):
-                dst.copy_(src, non_blocking=True)
-            gdn.decode.kernel(d_in[0], d_in[1], d_in[2], d_in[5], A_log, d_in[3], dt_bias, d_in[4], scale, out,
-                              d_in[5])
-            hout.copy_(out, non_blocking=True)
-            hns.copy_(d_in[5], non_blocking=True)
+        def dec_launch(j, d):  # in place: the state buffer is also new_state
+            gdn.decode.kernel(d[0], d[1], d[2], d[5], A_log, d[3], dt_bias, d[4], scale, dec_out[j], d[5])
+            return [dec_out[j], d[5]]
 
-        for _ in range(2):
-            e2e_step()
-        barrier()
-        ev0.record()
-        for _ in range(n_e2e):
-            e2e_step()
-        ev1.record()
-        barrier()
-        e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / n_e2e)
+        h2d = sum(t.numel() * t.element_size() for t in h_dec)
+        d2h = out.numel() * out.element_size() + states[0].numel() * 4
+        e2e_ms = pipelined_e2e(h_dec, dec_launch, n_e2e)
         e2e = {"value": round(world * DECODE_STATE_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
-               "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+               "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "pipeline": "copy-in / compute / copy-out streams, 3 buffer sets, pinned host memory"}
 
-        hp = [t.cpu().pin_memory() for t in (pq, pk, pv, pa, pb, ph0)]
-        dp = [torch.empty_like(t, device=dev) for t in hp]
-        hpo = torch.empty(pout.shape, dtype=pout.dtype).pin_memory()
-        hpn = torch.empty(pns.shape, dtype=torch.float32).pin_memory()
-        hcu = torch.tensor([0, T], dtype=torch.int32).pin_memory()
-        dcu = torch.empty_like(hcu, device=dev)
-        ph2d = sum(t.numel() * t.element_size() for t in hp) + hcu.numel() * 4
-        pd2h = hpo.numel() * 2 + hpn.numel() * 4
+        hcu = torch.tensor([0, T], dtype=torch.int32)
+        h_pre = [t.cpu().pin_memory() for t in (pq, pk, pv, pa, pb, ph0)] + [hcu.pin_memory()]
+        pre_out = [(torch.empty_like(pout), torch.empty_like(pns)) for _ in range(3)]
 
-        def pre_e2e_step():
-            for dst, src in zip(dp, hp):
-                dst.copy_(src, non_blocking=True)
-            dcu.copy_(hcu, non_blocking=True)
-            gdn.prefill.kernel(dp[0], dp[1], dp[2], dp[5], A_log, dp[3], dt_bias, dp[4], dcu, scale, pout, pns)
-            hpo.copy_(pout, non_blocking=True)
-            hpn.copy_(pns, non_blocking=True)
+        def pre_launch(j, d):
+            o, s_ = pre_out[j]
+            gdn.prefill.kernel(d[0], d[1], d[2], d[5], A_log, d[3], dt_bias, d[4], d[6], scale, o, s_)
+            return [o, s_]
 
-        for _ in range(2):
-            pre_e2e_step()
-        barrier()
-        ev0.record()
-        for _ in range(n_e2e):
-            pre_e2e_step()
-        ev1.record()
-        barrier()
-        pe_ms = max_over_ranks(ev0.elapsed_time(ev1) / n_e2e)
+        ph2d = sum(t.numel() * t.element_size() for t in h_pre)
+        pd2h = pout.numel() * 2 + pns.numel() * 4
+        pe_ms = pipelined_e2e(h_pre, pre_launch, n_e2e)
         pre_e2e = {"value": round(world * T / (pe_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(pe_ms, 4),
-                   "h2d_bytes_per_step": ph2d, "d2h_bytes_per_step": pd2h}
+                   "h2d_bytes_per_step": ph2d, "d2h_bytes_per_step": pd2h,
+                   "pipeline": "copy-in / compute / copy-out streams, 3 buffer sets, pinned host memory"}
 
     # ---------------- report ----------------
     if rank != 0:
