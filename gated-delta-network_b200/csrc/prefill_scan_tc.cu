@@ -212,15 +212,22 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
                         GDN_PH_ACC(dbg, 25, tp);
                         if (r < 64) {
                             // vn = (u - w h) e^{G_L - G_r} / |k_r|  -> bf16 hi + lo (MN-major SW128, token row r)
-                            const float ed = __expf(GL - G4[r * 4]) * G4[r * 4 + 3];
+                            const float4 g4r = *reinterpret_cast<const float4*>(G4 + r * 4);  // {G, e^G, beta, rk}
+                            const float ed = __expf(GL - g4r.x) * g4r.w;
                             const float* Us = reinterpret_cast<const float*>(st + kOffU);
                             unsigned char* rh = sm + kOffVh + r * 128;
                             unsigned char* rl = sm + kOffVl + r * 128;
+                            // Row r's 8 u values are 32 contiguous bytes.  Threads with bit 2 of r set
+                            // read the upper 16 bytes first, so each 8-thread phase of a 16-byte load
+                            // touches 8 different bank groups (no 2-way conflict).
+                            const int hA = (r >> 2) & 1;
 #pragma unroll
                             for (int jj = 0; jj < 4; ++jj) {
                                 const int j = 4 * half + jj;
-                                const float4 ua = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8);
-                                const float4 ub = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8 + 4);
+                                const float4 x0 = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8 + 4 * hA);
+                                const float4 x1 = *reinterpret_cast<const float4*>(Us + (j * 64 + r) * 8 + 4 * (hA ^ 1));
+                                const float4 ua = hA ? x1 : x0;
+                                const float4 ub = hA ? x0 : x1;
                                 const float uu[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
                                 uint32_t hi[4], lo[4];
 #pragma unroll

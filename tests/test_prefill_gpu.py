@@ -364,3 +364,43 @@ def test_prefill_only_short_single_launch(lens, cu):
     torch.cuda.synchronize()
     util.check_out(util.bits(o2), util.bits(out), atol=2e-3, rtol=2e-2)
     util.check_state(s2.cpu().numpy(), ns.cpu().numpy(), rel_l2=1e-4)
+
+
+def _all_same_inputs(T):
+    """The adversarial input noted for the reference's fast path (every tensor 0.5): with |k|^2 = 32
+    the delta rule multiplies the state by ~-19 per token, so the sequential oracle reaches ~1e22
+    at 64 tokens and overflows near 100."""
+    half = np.uint16(0x3F00)  # 0.5 in bf16
+    return dict(q=np.full((T, 4, 128), half), k=np.full((T, 4, 128), half), v=np.full((T, 8, 128), half),
+                state=np.full((1, 8, 128, 128), 0.5, np.float32), A_log=np.full(8, 0.5, np.float32),
+                a=np.full((T, 8), half), dt_bias=np.full(8, 0.5, np.float32), b=np.full((T, 8), half),
+                cu_seqlens=np.array([0, T], np.int32), scale=0.5)
+
+
+@pytest.mark.parametrize("T,flags", [(8, 0), (8, 2), (24, 0), (64, 0)],
+                         ids=["8_recurrent", "8_chunked", "24_short_tc", "64_chunked"])
+def test_prefill_all_same_input_stays_finite(T, flags):
+    """Every route stays finite where the oracle does (the reference's chunked path returns NaN
+    here).  The token recurrence matches at the usual bar; the chunked forms, whose inverse
+    (I + A)^-1 has entries ~20^n on this input, stay within 1% of the output's scale and 1e-2 state
+    rel-L2."""
+    from gdn import prefill as pmod
+
+    inp = _all_same_inputs(T)
+    args = util.prefill_args(inp)
+    out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(1, 8, 128, 128, dtype=torch.float32, device="cuda")
+    pmod._launch(*args, out, ns, flags=flags)
+    torch.cuda.synchronize()
+    ro, rs = _oracle(inp)
+    got = util.bf16_bits_to_f32(util.bits(out)).astype(np.float64)
+    ref = util.bf16_bits_to_f32(ro).astype(np.float64)
+    st, rs64 = ns.cpu().numpy().astype(np.float64), rs.astype(np.float64)
+    assert np.isfinite(got).all() and np.isfinite(st).all()
+    rel_state = np.linalg.norm(st - rs64) / np.linalg.norm(rs64)
+    if T == 8 and flags == 0:  # token-recurrent short kernel
+        util.check_out(util.bits(out), ro)
+        assert rel_state < util.STATE_REL_L2
+    else:
+        assert np.abs(got - ref).max() <= 1e-2 * np.abs(ref).max()
+        assert rel_state < 1e-2
