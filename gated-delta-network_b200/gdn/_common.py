@@ -1,6 +1,7 @@
 """Argument normalisation shared by the decode and prefill entry points."""
 from __future__ import annotations
 
+import contextlib
 import math
 
 import torch
@@ -43,6 +44,9 @@ def cuda_device(t: torch.Tensor, name: str) -> torch.device:
 def as_dev(t: torch.Tensor, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
     """Contiguous, 16-byte aligned tensor of `dtype` on `device` (copies only when needed: the
     library reads its inputs with TMA tile copies, which need 16-byte aligned bases)."""
+    if (t.dtype is dtype and t.is_cuda and t.get_device() == device.index and t.is_contiguous()
+            and not t.data_ptr() & 15):
+        return t  # the common case: nothing to convert (checked with cheap attribute reads)
     if t.device != device or t.dtype != dtype:
         t = t.to(device=device, dtype=dtype)
     t = t.contiguous()
@@ -55,5 +59,23 @@ def ptr(t):
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
+    """cudaStream_t of the current torch stream on `device`."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def on_device(device: torch.device):
+    """Make `device` current for the library call (a no-op context when it already is)."""
+    if torch.cuda.current_device() == device.index:
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
+def out_ok(t, device: torch.device, dtype: torch.dtype, numel: int) -> bool:
+    return (isinstance(t, torch.Tensor) and t.is_cuda and t.get_device() == device.index and t.dtype is dtype
+            and t.is_contiguous() and t.numel() == numel)

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._common import HEAD_DIM, as_dev, check_heads, cuda_device, ptr, resolve_scale, stream_handle
+from ._common import HEAD_DIM, as_dev, check_heads, cuda_device, on_device, out_ok, ptr, resolve_scale, stream_handle
 
 
 def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, flags=0):
@@ -43,16 +43,15 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, flag
         st = as_dev(state, torch.float32, dev)
     for name, t, shape, dt in (("output", output, (B, HV * V), torch.bfloat16),
                                ("new_state", new_state, (B, HV * V * K), torch.float32)):
-        if t.device != dev or t.dtype != dt or not t.is_contiguous() or t.numel() != shape[0] * shape[1]:
+        if not out_ok(t, dev, dt, shape[0] * shape[1]):
             raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor with {shape[0] * shape[1]} elements")
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with on_device(dev):
         rc = lib.gdn_decode_fwd(ptr(q_), ptr(k_), ptr(v_), ptr(st), ptr(A_), ptr(a_), ptr(d_), ptr(b_), s,
                                 ptr(output), ptr(new_state), B, Hq, HV, K, V, stream_handle(dev), flags)
     _lib.check("gdn_decode_fwd", rc)
 
 
-@torch.no_grad()
 def run(q, k, v, state, A_log, a, dt_bias, b, scale, *, use_qk_l2norm_in_kernel=False):
     """One decode step.  Returns ``(output [B,1,8,128] bf16, new_state [B,8,128,128] fp32)``.
 
@@ -74,7 +73,6 @@ def run(q, k, v, state, A_log, a, dt_bias, b, scale, *, use_qk_l2norm_in_kernel=
     return output, new_state
 
 
-@torch.no_grad()
 def kernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, *, use_qk_l2norm_in_kernel=False):
     """Destination-passing decode: writes ``output`` and ``new_state`` (which may be ``state`` itself)."""
     _launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state,

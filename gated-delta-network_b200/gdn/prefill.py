@@ -14,7 +14,8 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._common import HEAD_DIM, NUM_QK_HEADS, NUM_V_HEADS, as_dev, check_heads, cuda_device, ptr, resolve_scale, stream_handle
+from ._common import (HEAD_DIM, NUM_QK_HEADS, NUM_V_HEADS, as_dev, check_heads, cuda_device, on_device, out_ok, ptr,
+                      resolve_scale, stream_handle)
 
 
 def workspace_bytes(num_seqs: int, total_tokens: int, num_qk_heads: int = NUM_QK_HEADS,
@@ -37,8 +38,9 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     s = resolve_scale(scale)
     if cu_seqlens.dtype not in (torch.int32, torch.int64):
         raise ValueError("cu_seqlens must be int32 or int64")
-    cu = cu_seqlens if cu_seqlens.device == dev else cu_seqlens.to(dev)
-    cu = cu.contiguous()
+    cu = cu_seqlens if (cu_seqlens.is_cuda and cu_seqlens.get_device() == dev.index) else cu_seqlens.to(dev)
+    if not cu.is_contiguous():
+        cu = cu.contiguous()
     q_ = as_dev(q, torch.bfloat16, dev)
     k_ = as_dev(k, torch.bfloat16, dev)
     v_ = as_dev(v, torch.bfloat16, dev)
@@ -57,7 +59,7 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
         st = as_dev(state, torch.float32, dev)
     for name, t, n, dt in (("output", output, T * HV * V, torch.bfloat16),
                            ("new_state", new_state, N * HV * V * K, torch.float32)):
-        if t.device != dev or t.dtype != dt or not t.is_contiguous() or t.numel() != n:
+        if not out_ok(t, dev, dt, n):
             raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor with {n} elements")
     lib = _lib.load()
     need = workspace_bytes(N, T, Hq, HV)
@@ -65,9 +67,9 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
         ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
     else:
         ws = workspace
-        if ws.device != dev or ws.numel() * ws.element_size() < need:
+        if not ws.is_cuda or ws.get_device() != dev.index or ws.numel() * ws.element_size() < need:
             raise ValueError(f"workspace must be a CUDA buffer of at least {need} bytes")
-    with torch.cuda.device(dev):
+    with on_device(dev):
         rc = lib.gdn_prefill_fwd(ptr(q_), ptr(k_), ptr(v_), ptr(st), ptr(A_), ptr(a_), ptr(d_), ptr(b_), ptr(cu),
                                  1 if cu.dtype == torch.int64 else 0, N, T, s, ptr(output), ptr(new_state),
                                  ptr(ws), need, Hq, HV, K, V, stream_handle(dev), flags)
@@ -81,7 +83,6 @@ def read_status(workspace: torch.Tensor) -> int:
     return int(workspace[:4].view(torch.int32).item())
 
 
-@torch.no_grad()
 def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2norm_in_kernel=False):
     """Varlen prefill.  Returns ``(output [T,8,128] bf16, new_state [N,8,128,128] fp32)``.
 
@@ -106,7 +107,6 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
     return output, new_state
 
 
-@torch.no_grad()
 def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
            use_qk_l2norm_in_kernel=False):
     """Destination-passing prefill: writes ``output`` and ``new_state`` (which may be ``state``)."""
