@@ -12,7 +12,7 @@ Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed
   * decode_sweep (config 1): B = 1 .. 512, each over rotating state buffers (>= 384 MiB), beside
     the reference's published latencies.
   * prefill_configs: single sequences of 64 .. 4096 tokens (beside the reference's published table),
-    one 1024-token sequence, 16 log-uniform varlen sequences (total <= 32768)
+    one 1024-token sequence, 1000 x 16 and 4000 x 6 short sequences (the short-sequence kernels), 16 log-uniform varlen sequences (total <= 32768)
     and 8 packed 1024-token sequences per GPU, timed the same way; plus 64 x 4096 tokens split by
     sequence over the ranks (strong scaling; whole-job tokens/s over the slowest rank).
   * e2e: the same two metrics through the public API (gdn.decode.kernel / gdn.prefill.kernel)
@@ -440,6 +440,9 @@ def main():
         "1x4096": dict(time_prefill([4096], True), reference_published_ms=0.420),
         "16 varlen, log-uniform [6, 8192] (config 3)": time_prefill(varlen_lengths(), True),
         "8x1024 packed": time_prefill([1024] * 8, True),
+        # batches of short prompts: the short-sequence kernels (one-chunk tensor-core / token recurrence)
+        "1000x16 short sequences": time_prefill([16] * 1000, True),
+        "4000x6 short sequences": time_prefill([6] * 4000, True),
         "64x4096 partitioned (config 4)": c4,
     }
 
