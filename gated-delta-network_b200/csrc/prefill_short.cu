@@ -395,19 +395,14 @@ __global__ void __launch_bounds__(shk::kThreads, 2) gdn_prefill_short_kernel(Pre
             ldsm_x4_tr(ah[ks], VHb + arow * kRS + acol);
             ldsm_x4_tr(al[ks], VLb + arow * kRS + acol);
         }
-        // two halves of 64 k-columns: the half's fp32 state rows are read (from L2) while its MMAs run
+        // Two halves of 64 k-columns.  The half's update block (16 state rows x 64 k per warp) goes
+        // through shared memory (the bf16 state copy is free by now: [128][68] fp32), so the fp32
+        // state is re-read (from L2) and written back with 16-byte row-contiguous accesses instead of
+        // the MMA fragment layout's 8-byte pieces spread over 8 rows.
+        float* Ss = reinterpret_cast<float*>(Sb);
+        constexpr int kSS = 68;  // fp32 row stride of the staging block
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-            float2 x[8], y[8];
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                const int k = 64 * hf + 8 * nt + 2 * tq;
-                x[nt] = y[nt] = make_float2(0.f, 0.f);
-                if (p.state) {
-                    x[nt] = *reinterpret_cast<const float2*>(p.state + shead + (size_t)va * kD + k);
-                    y[nt] = *reinterpret_cast<const float2*>(p.state + shead + (size_t)vb * kD + k);
-                }
-            }
             float acc[8][4];
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt)
@@ -425,13 +420,23 @@ __global__ void __launch_bounds__(shk::kThreads, 2) gdn_prefill_short_kernel(Pre
                     mma_bf16(acc[2 * np], al[ks], b[0], b[1]);
                     mma_bf16(acc[2 * np + 1], al[ks], b[2], b[3]);
                 }
+            if (hf == 1) __syncwarp();  // this warp's reads of the first half's block are done
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) {
-                const int k = 64 * hf + 8 * nt + 2 * tq;
-                *reinterpret_cast<float2*>(p.new_state + shead + (size_t)va * kD + k) =
-                    make_float2(fmaf(gL, x[nt].x, acc[nt][0]), fmaf(gL, x[nt].y, acc[nt][1]));
-                *reinterpret_cast<float2*>(p.new_state + shead + (size_t)vb * kD + k) =
-                    make_float2(fmaf(gL, y[nt].x, acc[nt][2]), fmaf(gL, y[nt].y, acc[nt][3]));
+                const int c = 8 * nt + 2 * tq;
+                *reinterpret_cast<float2*>(Ss + va * kSS + c) = make_float2(acc[nt][0], acc[nt][1]);
+                *reinterpret_cast<float2*>(Ss + vb * kSS + c) = make_float2(acc[nt][2], acc[nt][3]);
+            }
+            __syncwarp();
+            // rows 16 warp .. +15, 16 float4 per row: lane covers float4 (lane & 15) of rows 2 i + (lane >> 4)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int v = 16 * warp + 2 * i + (lane >> 4), c4 = 4 * (lane & 15);
+                const size_t g = shead + (size_t)v * kD + 64 * hf + c4;
+                const float4 s0 = p.state ? *reinterpret_cast<const float4*>(p.state + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 d = *reinterpret_cast<const float4*>(Ss + v * kSS + c4);
+                st_stream_f4(p.new_state + g, make_float4(fmaf(gL, s0.x, d.x), fmaf(gL, s0.y, d.y),
+                                                          fmaf(gL, s0.z, d.z), fmaf(gL, s0.w, d.w)));
             }
         }
     }
