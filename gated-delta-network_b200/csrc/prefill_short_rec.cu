@@ -116,14 +116,21 @@ __global__ void __launch_bounds__(kRecThreads) gdn_prefill_short_rec_kernel(Pref
             kv[i] = *reinterpret_cast<const float4*>(&sk_[t][32 * i + 4 * j]);
         }
         const float g = sg_[t], beta = sb_[t], kq = skq_[t];
-        float ska = 0.f, sqa = 0.f, skb = 0.f, sqb = 0.f;
+        // Lane-paired fp32 (f32x2): the four dot products and the update run on element pairs,
+        // halving the instruction count of this instruction-bound loop.
+        float2 aka = make_float2(0.f, 0.f), aqa = aka, akb = aka, aqb = aka;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            ska = fmaf(Sa[i].x, kv[i].x, fmaf(Sa[i].y, kv[i].y, fmaf(Sa[i].z, kv[i].z, fmaf(Sa[i].w, kv[i].w, ska))));
-            sqa = fmaf(Sa[i].x, qv[i].x, fmaf(Sa[i].y, qv[i].y, fmaf(Sa[i].z, qv[i].z, fmaf(Sa[i].w, qv[i].w, sqa))));
-            skb = fmaf(Sb[i].x, kv[i].x, fmaf(Sb[i].y, kv[i].y, fmaf(Sb[i].z, kv[i].z, fmaf(Sb[i].w, kv[i].w, skb))));
-            sqb = fmaf(Sb[i].x, qv[i].x, fmaf(Sb[i].y, qv[i].y, fmaf(Sb[i].z, qv[i].z, fmaf(Sb[i].w, qv[i].w, sqb))));
+            const float2 k0 = make_float2(kv[i].x, kv[i].y), k1 = make_float2(kv[i].z, kv[i].w);
+            const float2 q0 = make_float2(qv[i].x, qv[i].y), q1 = make_float2(qv[i].z, qv[i].w);
+            const float2 a0 = make_float2(Sa[i].x, Sa[i].y), a1 = make_float2(Sa[i].z, Sa[i].w);
+            const float2 b0 = make_float2(Sb[i].x, Sb[i].y), b1 = make_float2(Sb[i].z, Sb[i].w);
+            aka = fma2(a1, k1, fma2(a0, k0, aka));
+            aqa = fma2(a1, q1, fma2(a0, q0, aqa));
+            akb = fma2(b1, k1, fma2(b0, k0, akb));
+            aqb = fma2(b1, q1, fma2(b0, q0, aqb));
         }
+        float ska = aka.x + aka.y, sqa = aqa.x + aqa.y, skb = akb.x + akb.y, sqb = aqb.x + aqb.y;
 #pragma unroll
         for (int off = 1; off < 8; off <<= 1) {
             ska += __shfl_xor_sync(0xffffffffu, ska, off);
@@ -133,16 +140,16 @@ __global__ void __launch_bounds__(kRecThreads) gdn_prefill_short_rec_kernel(Pref
         }
         const float vna = beta * (bf2f(sv_[t][ra]) - g * ska);
         const float vnb = beta * (bf2f(sv_[t][rb]) - g * skb);
+        const float2 g2 = make_float2(g, g), va2 = make_float2(vna, vna), vb2 = make_float2(vnb, vnb);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            Sa[i].x = fmaf(g, Sa[i].x, vna * kv[i].x);
-            Sa[i].y = fmaf(g, Sa[i].y, vna * kv[i].y);
-            Sa[i].z = fmaf(g, Sa[i].z, vna * kv[i].z);
-            Sa[i].w = fmaf(g, Sa[i].w, vna * kv[i].w);
-            Sb[i].x = fmaf(g, Sb[i].x, vnb * kv[i].x);
-            Sb[i].y = fmaf(g, Sb[i].y, vnb * kv[i].y);
-            Sb[i].z = fmaf(g, Sb[i].z, vnb * kv[i].z);
-            Sb[i].w = fmaf(g, Sb[i].w, vnb * kv[i].w);
+            const float2 k0 = make_float2(kv[i].x, kv[i].y), k1 = make_float2(kv[i].z, kv[i].w);
+            const float2 a0 = fma2(g2, make_float2(Sa[i].x, Sa[i].y), mul2(va2, k0));
+            const float2 a1 = fma2(g2, make_float2(Sa[i].z, Sa[i].w), mul2(va2, k1));
+            const float2 b0 = fma2(g2, make_float2(Sb[i].x, Sb[i].y), mul2(vb2, k0));
+            const float2 b1 = fma2(g2, make_float2(Sb[i].z, Sb[i].w), mul2(vb2, k1));
+            Sa[i] = make_float4(a0.x, a0.y, a1.x, a1.y);
+            Sb[i] = make_float4(b0.x, b0.y, b1.x, b1.y);
         }
         if (j == 0) {
             uint16_t* o = p.out + ((size_t)(bos + t) * p.HV + hv) * kD;
