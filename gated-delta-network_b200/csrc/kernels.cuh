@@ -39,7 +39,7 @@ struct PrefillArgs {
     int H, HV;             // q/k heads and v heads (HV a multiple of H and of 8; 4 and 8 in the reference)
     int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
     int test_withhold;     // GDN_FLAG_TEST_WITHHOLD_CHUNK: the scan skips chunk 1's copies
-    int short_path;        // 1: sequences of 0..kShortLen tokens go to the recurrent short kernel, and
+    int short_path;        // 1: sequences of 0..kShortLen tokens go to a short-sequence kernel, and
                            //    the chunked kernels see only the compacted list of the longer ones
     int rows;              // sequences the scan grid covers (N, or with short_path a bound on the
                            // number of longer sequences: min(N, T / (kShortLen + 1)), at least 1)
