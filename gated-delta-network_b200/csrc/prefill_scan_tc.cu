@@ -232,10 +232,13 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
                                 uint32_t hi[4], lo[4];
 #pragma unroll
                                 for (int e = 0; e < 4; ++e) {
-                                    const float x0 = (uu[2 * e] - __uint_as_float(d[8 * jj + 2 * e])) * ed;
-                                    const float x1 = (uu[2 * e + 1] - __uint_as_float(d[8 * jj + 2 * e + 1])) * ed;
-                                    hi[e] = pack_bf16x2(x0, x1);
-                                    lo[e] = pack_bf16x2(x0 - __uint_as_float(hi[e] << 16), x1 - __uint_as_float(hi[e] & 0xffff0000u));
+                                    const float2 x = mul2(sub2(make_float2(uu[2 * e], uu[2 * e + 1]),
+                                                               make_float2(__uint_as_float(d[8 * jj + 2 * e]),
+                                                                           __uint_as_float(d[8 * jj + 2 * e + 1]))),
+                                                          make_float2(ed, ed));
+                                    hi[e] = pack_bf16x2(x.x, x.y);
+                                    const float2 r2 = sub2(x, make_float2(__uint_as_float(hi[e] << 16), __uint_as_float(hi[e] & 0xffff0000u)));
+                                    lo[e] = pack_bf16x2(r2.x, r2.y);
                                 }
                                 *reinterpret_cast<uint4*>(rh + ((j ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                                 *reinterpret_cast<uint4*>(rl + ((j ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
@@ -275,8 +278,12 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
                                 uint32_t pk[4];
 #pragma unroll
                                 for (int e = 0; e < 4; ++e)
-                                    pk[e] = pack_bf16x2(p.scale * (__uint_as_float(d[8 * jj + 2 * e]) + __uint_as_float(ow[e] << 16)),
-                                                        p.scale * (__uint_as_float(d[8 * jj + 2 * e + 1]) + __uint_as_float(ow[e] & 0xffff0000u)));
+                                {
+                                    const float2 o2 = mul2(make_float2(p.scale, p.scale),
+                                                           add2(make_float2(__uint_as_float(d[8 * jj + 2 * e]), __uint_as_float(d[8 * jj + 2 * e + 1])),
+                                                                make_float2(__uint_as_float(ow[e] << 16), __uint_as_float(ow[e] & 0xffff0000u))));
+                                    pk[e] = pack_bf16x2(o2.x, o2.y);
+                                }
                                 *reinterpret_cast<uint4*>(ob + ((j ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                             }
                             named_bar_sync(3, 128);  // the four output warps
@@ -302,7 +309,12 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
                         tmem_regs_ready(d);
                         const float eL = __expf(GL);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) h[j] = fmaf(eL, h[j], __uint_as_float(d[j]));
+                        for (int j = 0; j < 32; j += 2) {  // lane-paired fp32, same values as fmaf per element
+                            const float2 hn = fma2(make_float2(eL, eL), make_float2(h[j], h[j + 1]),
+                                                   make_float2(__uint_as_float(d[j]), __uint_as_float(d[j + 1])));
+                            h[j] = hn.x;
+                            h[j + 1] = hn.y;
+                        }
                     }
                     // the stage's smem operands and TMEM results are consumed: hand the stage back
                     __syncwarp();
