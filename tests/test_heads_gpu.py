@@ -30,11 +30,11 @@ def test_decode_head_families_match_oracle(h, hv, B):
 
 
 PREFILL_FAMILIES = [(16, 32), (8, 16), (2, 8), (8, 8), (4, 16)]
-PREFILL_LENS = [[200], [64, 1, 0, 130], [6] * 36 + [90], [20] * 36 + [90]]
+PREFILL_LENS = [[200], [64, 1, 0, 130], [6] * 36 + [90], [20] * 36 + [90], [5, 9, 0, 12], [20]]
 
 
 @pytest.mark.parametrize("h,hv", PREFILL_FAMILIES, ids=[f"qk{h}_v{v}" for h, v in PREFILL_FAMILIES])
-@pytest.mark.parametrize("lens", PREFILL_LENS, ids=["200", "mixed4", "short37", "short37tc"])
+@pytest.mark.parametrize("lens", PREFILL_LENS, ids=["200", "mixed4", "short37", "short37tc", "only_short_rec", "only_short_tc"])
 def test_prefill_head_families_match_oracle(h, hv, lens):
     inp = gi.prefill_inputs(lens, seed=600 + h + hv + len(lens), h=h, hv=hv)
     out, ns = gdn.prefill.run(*util.prefill_args(inp))

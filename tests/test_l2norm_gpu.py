@@ -39,10 +39,10 @@ def test_decode_l2norm_in_place_dps():
     util.check_state(st.cpu().numpy(), rs, rel_l2=1e-5)
 
 
-PREFILL_CASES = [[1], [64], [200], [130, 0, 77, 300], [1024], [6] * 40 + [100, 3, 70], [20] * 40 + [100, 3, 70]]
+PREFILL_CASES = [[1], [64], [200], [130, 0, 77, 300], [1024], [6] * 40 + [100, 3, 70], [20] * 40 + [100, 3, 70], [24]]
 
 
-@pytest.mark.parametrize("lens", PREFILL_CASES, ids=["1", "64", "200", "mixed4", "1024", "short43", "short43tc"])
+@pytest.mark.parametrize("lens", PREFILL_CASES, ids=["1", "64", "200", "mixed4", "1024", "short43", "short43tc", "only_short_tc"])
 def test_prefill_l2norm_matches_oracle(lens):
     inp = gi.prefill_inputs(lens, seed=400 + len(lens), normalized=False)
     out, ns = gdn.prefill.run(*util.prefill_args(inp), use_qk_l2norm_in_kernel=True)

@@ -54,8 +54,12 @@ def test_prefill_matches_reference_golden(name, fx):
     check.compare(fx, "state", ns.cpu().numpy(), atol=1e-3, rtol=1e-2, proj_rtol=1e-3)
 
 
-def test_prefill_int64_cu_seqlens():
-    inp = gi.prefill_inputs([70, 33, 129], seed=21)
+@pytest.mark.parametrize("lens", [[70, 33, 129], [1, 24, 25, 3, 200, 0, 17] * 6, [6] * 40, [5, 20]],
+                         ids=["mma_sync_scan", "short_path_persistent", "short_rec", "only_short"])
+def test_prefill_int64_cu_seqlens(lens):
+    """int64 cu_seqlens give bit-identical results to int32 on every route (chunked, short path with
+    the chunk table and persistent grids, token recurrence, single-launch short kernel)."""
+    inp = gi.prefill_inputs(lens, seed=21)
     o32, s32 = gdn.prefill.run(*util.prefill_args(inp, cu_dtype=torch.int32))
     o64, s64 = gdn.prefill.run(*util.prefill_args(inp, cu_dtype=torch.int64))
     torch.cuda.synchronize()
