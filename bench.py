@@ -53,6 +53,7 @@ DECODE_ALG_BYTES = DECODE_B * (2 * STATE_BYTES_PER_ELEM + 2 * H * D * 2 + 2 * HV
 PREFILL_ALG_BYTES_PER_TOKEN = 2 * H * D * 2 + HV * D * 2 + 2 * HV * 2 + HV * D * 2   # 6,176 B
 PREFILL_FLOPS_PER_TOKEN = (10 * 64 * 128 + 6 * 128 * 128) * HV                      # chunked WY form, 1,441,792
 N_STATE_BUFS = 8
+REPS = 5  # timed repetitions of every measurement; the median is reported
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum), or None.
 # Source: the ncu summaries under profiles/ (decode B=64 launch; prefill kernels at T=8192).
 # decode: 33.83 MB read; the 33.55 MB of state writes are still dirty in L2 when ncu's replayed launch ends.
@@ -181,34 +182,72 @@ def cpu_prefill_baseline(tokens=1024, threads=0):
                       f"the sequential oracle's cost is linear in tokens"}
 
 
+def bind_host_to_gpu(dev_index):
+    """Restrict this process to the CPUs local to its GPU's PCIe root (sysfs local_cpulist), so
+    that pinned host buffers are first touched -- and placed -- on the GPU's own NUMA node.
+    Returns a description for the JSON line."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(dev_index)
+        bdf = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        base = f"/sys/bus/pci/devices/{bdf}"
+        with open(base + "/local_cpulist") as f:
+            cpulist = f.read().strip()
+        try:
+            with open(base + "/numa_node") as f:
+                node = int(f.read().strip())
+        except OSError:
+            node = -1
+        cpus = set()
+        for part in cpulist.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return {"pci": bdf, "numa_node": node, "cpus": cpulist}
+    except Exception as exc:  # sysfs layout differs: keep the default placement
+        return {"unbound": str(exc)[:80]}
+
+
+def decode_config(world):
+    """Workload of the headline line, shared by both arms (the same dict in each)."""
+    return {"workload": "decode B=64 per GPU (qk4_v8_d128, k-last fp32 state, in place), one step",
+            "global_batch": DECODE_B * world, "seq_len": 1,
+            "parallelism": f"dp{world}: the global batch in {world} independent shards"}
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
     from oracle import oracle
 
     threads = host_threads()
-    for _ in range(args.warmup):
-        cpu_decode_baseline(budget_s=0.0, threads=threads)
     times = []
     from tests.golden import inputs as gi
 
-    inp = gi.decode_inputs(DECODE_B, seed=0)
+    # the same global batch as the GPU arm: B = 64 per GPU x N GPUs, on the host cores
+    gb = DECODE_B * world
+    inp = gi.decode_inputs(gb, seed=0)
     a = (inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"])
+    for _ in range(args.warmup):
+        oracle.decode(*a, threads=threads)
     for _ in range(args.steps):
         t0 = time.perf_counter()
         oracle.decode(*a, threads=threads)
         times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
-    val = DECODE_STATE_BYTES / per / 1e9
+    val = world * DECODE_STATE_BYTES / per / 1e9
     line = {
         "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decode B=64 (qk4_v8_d128, k-last fp32 state), one step", "global_batch": DECODE_B,
-                   "seq_len": 1, "parallelism": "none (rank 0 only, host cores)"},
+        "config": decode_config(world),
+        "timing": f"host wall clock (time.perf_counter) per step, mean of --steps steps, rank 0 only",
         "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} full decode steps at B=64 of the C restatement of "
-                                   f"reference/gdn_decode_ref.py, {threads} threads"},
+                         "sample": f"{args.steps} full decode steps at B={gb} (the whole global batch) of the C "
+                                   f"restatement of reference/gdn_decode_ref.py, {threads} threads"},
         "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -242,6 +281,8 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    orig_affinity = os.sched_getaffinity(0)
+    host_binding = bind_host_to_gpu(local_rank)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
 
@@ -283,34 +324,52 @@ def main():
         st = states[i % N_STATE_BUFS]
         gdn.decode.kernel(q, k, v, st, A_log, a, dt_bias, b, scale, out, st)
 
-    # CUDA graph of N_STATE_BUFS launches (one per buffer)
+    # CUDA graph of exactly K = --steps launches, cycling over the N_STATE_BUFS state buffers.
     side = torch.cuda.Stream(device=dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
         for i in range(N_STATE_BUFS):
             decode_step(i)
     torch.cuda.current_stream(dev).wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for i in range(N_STATE_BUFS):
-            decode_step(i)
-    reps = max(1, args.steps // N_STATE_BUFS)
-    steps = reps * N_STATE_BUFS
-    for _ in range(max(1, args.warmup // N_STATE_BUFS + 1)):
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                decode_step(i)
+        return g
+
+    steps = args.steps
+    graph = capture(steps)
+    # >= 10 ms of launches in one region, the stability cross-check of the K-step number
+    n_long = max(N_STATE_BUFS, -(-int(10e-3 / 11e-6) // N_STATE_BUFS) * N_STATE_BUFS)
+    graph_long = capture(n_long)
+    for _ in range(args.warmup):
         graph.replay()
+    graph_long.replay()
     barrier()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
+
+    def timed_replay(g, n):
+        """Device time per launch of one replay of `g` (n launches).  A ~1 ms sleep kernel queued
+        first keeps the GPU busy while the host submits the graph, so the region holds the
+        launches back to back and no host submission latency."""
         barrier()
+        torch.cuda._sleep(2_000_000)
         ev0.record()
-        for _ in range(reps):
-            graph.replay()
+        g.replay()
         ev1.record()
         barrier()
-    dec_ms = ev0.elapsed_time(ev1) / steps
-    dec_ms = max_over_ranks(dec_ms)
+        return ev0.elapsed_time(ev1) / n
+
+    with ClockSampler(local_rank) as clocks:
+        rep_ms = [max_over_ranks(timed_replay(graph, steps)) for _ in range(REPS)]
+        long_ms = [max_over_ranks(timed_replay(graph_long, n_long)) for _ in range(REPS)]
+    dec_ms = statistics.median(rep_ms)
+    dec_long_ms = statistics.median(long_ms)
     clock_summary = clocks.summary()
+    del graph_long
 
     # eager launches (Python + ctypes path, no graph)
     barrier()
@@ -341,13 +400,17 @@ def main():
                 gdn.decode.kernel(sq, sk, sv, st, A_log, sa, dt_bias, sb, scale, so, st)
         reps = max(2, 400 // nb)
         g.replay()
-        barrier()
-        ev0.record()
-        for _ in range(reps):
-            g.replay()
-        ev1.record()
-        barrier()
-        ms = max_over_ranks(ev0.elapsed_time(ev1) / (reps * nb))
+        per_rep = []
+        for _ in range(REPS):
+            barrier()
+            torch.cuda._sleep(2_000_000)
+            ev0.record()
+            for _ in range(reps):
+                g.replay()
+            ev1.record()
+            barrier()
+            per_rep.append(max_over_ranks(ev0.elapsed_time(ev1) / (reps * nb)))
+        ms = statistics.median(per_rep)
         del g, sts
         return {"us_per_step": round(ms * 1e3, 3), "state_GBps": round(2 * sbytes / (ms * 1e-3) / 1e9, 1),
                 "frac_of_hbm_peak": round(2 * sbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4)}
@@ -357,6 +420,17 @@ def main():
     decode_sweep = {}
     for bs in (1, 4, 8, 16, 32, 48, 64, 128, 512):
         decode_sweep[f"B={bs}"] = dict(time_decode(bs), reference_published_us=ref_decode_us[bs])
+
+    # config 4, decode half: B = 512 split by batch over the ranks (strong scaling, no collective);
+    # whole-job state traffic over the slowest rank's time per step
+    from gdn.shard import batch_shard
+
+    b0, b1 = batch_shard(512, world, rank)
+    c4d = time_decode(b1 - b0)
+    c4_dec = {"us_per_step": c4d["us_per_step"], "local_batch": b1 - b0,
+              "state_GBps_whole_job": round(512 * STATE_BYTES_PER_ELEM * 2 / (c4d["us_per_step"] * 1e-6) / 1e9, 1),
+              "frac_of_hbm_peak_per_gpu": c4d["frac_of_hbm_peak"],
+              "scaling": "strong: decode B=512 split by batch over the ranks"}
 
     # ---------------- prefill 8K ----------------
     T = PREFILL_T
@@ -387,7 +461,7 @@ def main():
         prefill_step()
         e1.record()
     barrier()
-    pre_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / len(evs)
+    pre_ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
     pre_ms = max_over_ranks(pre_ms)
 
     # ---------------- other prefill configurations (reported alongside) ----------------
@@ -415,7 +489,7 @@ def main():
             step()
             e1.record()
         barrier()
-        ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps)
+        ms = max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs))
         return {"tokens_per_s": round(world * Tn / (ms * 1e-3), 1), "ms_per_step": round(ms, 5), "tokens": Tn,
                 "sequences": Nn}
 
@@ -444,6 +518,42 @@ def main():
         "1000x16 short sequences": time_prefill([16] * 1000, True),
         "4000x6 short sequences": time_prefill([6] * 4000, True),
         "64x4096 partitioned (config 4)": c4,
+    }
+
+    # FlashInfer-Bench style timing: every argument (inputs and the destination tensors) is cloned
+    # before each iteration inside the timed region, then the public destination-passing call runs
+    # (the reference's published clone-mode table, README.md:115-120).
+    def time_prefill_clone(T_, steps=20):
+        xq, xk = l2n(randn((T_, H, D))), l2n(randn((T_, H, D)))
+        xv = randn((T_, HV, D), dtype=torch.bfloat16)
+        xa, xb = randn((T_, HV), dtype=torch.bfloat16), randn((T_, HV), dtype=torch.bfloat16)
+        xh = randn((1, HV, D, D), 0.02)
+        xcu = torch.tensor([0, T_], dtype=torch.int32, device=dev)
+        xo = torch.empty((T_, HV, D), dtype=torch.bfloat16, device=dev)
+        xs = torch.empty((1, HV, D, D), dtype=torch.float32, device=dev)
+        argl = [xq, xk, xv, xh, A_log, xa, dt_bias, xb, xcu, xo, xs]
+
+        def it():
+            c = [t.clone() for t in argl]
+            gdn.prefill.kernel(c[0], c[1], c[2], c[3], c[4], c[5], c[6], c[7], c[8], scale, c[9], c[10])
+
+        for _ in range(3):
+            it()
+        barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            e0.record()
+            it()
+            e1.record()
+        barrier()
+        ms = max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs))
+        return {"ms_per_step": round(ms, 5), "tokens_per_s": round(world * T_ / (ms * 1e-3), 1)}
+
+    prefill_clone = {
+        "1x1024": dict(time_prefill_clone(1024), reference_published_clone_ms=0.546),
+        "1x4096": dict(time_prefill_clone(4096), reference_published_clone_ms=0.805),
+        "method": "median of 20 iterations; each clones all 11 tensor arguments, then calls gdn.prefill.kernel, "
+                  "both inside the CUDA-event region (FlashInfer-Bench do_bench _clone_args)",
     }
 
     # ---------------- e2e through the public API with pinned host buffers ----------------
@@ -496,9 +606,33 @@ def main():
         barrier()
         return max_over_ranks(t0.elapsed_time(t1) / n_steps)
 
+    def host_link_rates(nbytes=64 << 20, reps=5):
+        """H2D and D2H copy rates of this rank from pinned memory, all ranks copying at the same
+        time (the e2e loop's situation): the per-rank numbers locate a shared host-side limit."""
+        hb = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        db = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        out = {}
+        for name, fn in (("h2d_GBps", lambda: db.copy_(hb, non_blocking=True)),
+                         ("d2h_GBps", lambda: hb.copy_(db, non_blocking=True))):
+            fn()
+            barrier()
+            ev0.record()
+            for _ in range(reps):
+                fn()
+            ev1.record()
+            barrier()
+            out[name] = round(reps * nbytes / (ev0.elapsed_time(ev1) * 1e-3) / 1e9, 2)
+        return out
+
     e2e = None
     pre_e2e = None
+    link = None
     if not args.no_e2e:
+        link = host_link_rates()
+        if world > 1:
+            allr = [None] * world
+            dist.all_gather_object(allr, {**link, **host_binding})
+            link = {"per_rank": allr}
         n_e2e = max(6, min(30, args.steps // 8))
         h_dec = [t.cpu().pin_memory() for t in (q, k, v, a, b, states[0])]
         dec_out = [torch.empty_like(out) for _ in range(3)]
@@ -537,6 +671,7 @@ def main():
             dist.destroy_process_group()
         return
     cpu = None
+    os.sched_setaffinity(0, orig_affinity)  # the CPU baselines use every core this process may run on
     if not args.no_cpu_baseline:
         cpu = cpu_decode_baseline(budget_s=args.cpu_budget)
         cpu_pre = cpu_prefill_baseline(8192)
@@ -559,13 +694,18 @@ def main():
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "decode B=64 per GPU (qk4_v8_d128, k-last fp32 state, in place), one step",
-                   "global_batch": DECODE_B * world, "seq_len": 1, "parallelism": f"dp{world} (independent shards)",
-                   "l2": f"{N_STATE_BUFS} rotating state buffers ({N_STATE_BUFS * 32} MiB > 126 MB L2)",
-                   "timing": "CUDA graph replays, CUDA events, max over ranks"},
+        "config": decode_config(world),
+        "l2": f"{N_STATE_BUFS} rotating state buffers ({N_STATE_BUFS * 32} MiB > 126 MB L2)",
+        "timing": f"median of {REPS} timed replays of a CUDA graph of exactly --steps launches "
+                  f"(each preceded by a sleep kernel so the launches run back to back), CUDA events, "
+                  f"max over ranks",
         "decode_us_per_step": round(dec_us, 3),
+        "decode_us_per_rep": [round(x * 1e3, 3) for x in rep_ms],
+        "decode_long_us_per_step": round(dec_long_ms * 1e3, 3),
+        "decode_long_launches": n_long,
         "decode_eager_us_per_step": round(dec_eager_ms * 1e3, 3),
         "decode_sweep": decode_sweep,
+        "decode_config4_b512": c4_dec,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": NCU_TRAFFIC["decode"],
                      "kernel": "gdn_decode_kernel", "peak_source": peak_src},
@@ -578,8 +718,10 @@ def main():
             "e2e": pre_e2e,
         },
         "prefill_configs": prefill_more,
+        "prefill_clone_mode": prefill_clone,
         "e2e": e2e,
-        "gpu_launches": steps,
+        "host_link": link if world > 1 else ({**link, **host_binding} if link else None),
+        "gpu_launches": steps * REPS,
         "clocks": clock_summary,
     }
     if cpu is not None:

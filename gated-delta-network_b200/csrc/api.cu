@@ -16,20 +16,34 @@
 namespace {
 
 constexpr int kMaxDevices = 64;
-// 0 = unknown, 1 = sm_100 family, 2 = other.  Benign race: every writer stores the same value.
+// 0 = unknown, 1 = compute capability 10.0, 2 = other.  Benign race: every writer stores the same value.
 int g_dev_ok[kMaxDevices];
 
+}  // namespace
+
+namespace gdn {
+
+// The library holds sm_100a code only: other compute capabilities (including sm_103 parts of
+// the same major) have no image to run, so they are refused here with GDN_ERR_DEVICE.
 int check_device() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return GDN_ERR_DEVICE;
     if (g_dev_ok[dev] == 0) {
-        int major = 0;
-        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return GDN_ERR_CUDA;
-        g_dev_ok[dev] = (major == 10) ? 1 : 2;
+        int major = 0, minor = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+            return GDN_ERR_CUDA;
+        g_dev_ok[dev] = (major == 10 && minor == 0) ? 1 : 2;
     }
     return g_dev_ok[dev] == 1 ? GDN_OK : GDN_ERR_DEVICE;
 }
+
+}  // namespace gdn
+
+namespace {
+
+using gdn::check_device;
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

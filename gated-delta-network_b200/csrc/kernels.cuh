@@ -71,6 +71,8 @@ struct PrefillLayout {
     size_t off_status, off_base, off_seq, off_long, off_w, off_u, off_qp, off_oi, off_g4, total;
 };
 
+// GDN_OK when the current device is compute capability 10.0 (B200), else a GDN_ERR_* code.
+int check_device();
 int launch_decode(const DecodeArgs& p, int variant, cudaStream_t stream);
 int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream);
 // Slots: one per 64-token chunk of each sequence.  sum_n ceil(len_n / 64) <= T/64 + N, and

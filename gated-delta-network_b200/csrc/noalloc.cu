@@ -10,7 +10,10 @@
 //
 // Host code may not pass the array's name to a kernel: on the host it is a stand-in symbol,
 // not a device address.  The device address is looked up once per device with
-// cudaGetSymbolAddress (with that device current) on the first call and cached.
+// cudaGetSymbolAddress (with that device current) on the first call and cached.  The cache
+// belongs to the device's primary context: a caller that resets the device (cudaDeviceReset)
+// destroys the array with the context and must not call this entry point on that device again
+// in the same process.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -37,6 +40,10 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
                                        const void* cu_seqlens, int cu_is_int64, int N, int T, float scale, void* out,
                                        float* new_state, int H, int HV, int K, int V, void* stream, unsigned flags) {
     if (T < 0 || N < 0 || T > GDN_NOALLOC_MAX_TOKENS || N > GDN_NOALLOC_MAX_SEQS) return GDN_ERR_SIZE;
+    // The device check comes before the symbol lookup: on a GPU without an sm_100a image the
+    // lookup itself would fail and report a CUDA error instead of the unsupported device.
+    const int drc = gdn::check_device();
+    if (drc != GDN_OK) return drc;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return GDN_ERR_DEVICE;

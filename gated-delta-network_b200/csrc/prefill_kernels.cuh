@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "sm100.cuh"
 
 namespace gdn {
 
@@ -100,6 +101,16 @@ __device__ __forceinline__ int warp_seq_by_rank(const PrefillArgs& p, int r) {
     }
     const unsigned hit = __ballot_sync(0xffffffffu, lane < p.N && rank == r);
     return hit ? __ffs(hit) - 1 : r;
+}
+
+// Chunks of one sequence that fit the workspace from its first slot.  cu_seqlens that is not
+// non-decreasing (overlapping sequences) can claim more chunks in total than the S slots hold;
+// the excess is skipped and reported (status word 0), so no workspace access leaves the buffer.
+__device__ __forceinline__ int clamp_chunks(const PrefillArgs& p, int slot0, int nchunks, bool report) {
+    const int room = p.S - slot0;
+    if (nchunks <= room) return nchunks;
+    if (report) atomicCAS(p.status, 0, kErrBadSeqlens);
+    return room > 0 ? room : 0;
 }
 
 bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m);

@@ -142,12 +142,18 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         tma_prefetch_desc(&maps.b);
     }
     pdl_wait();  // inputs and the chunk table come from earlier work on the stream
+    // Without a chunk-table kernel this is the call's first kernel: reset the status word here,
+    // before any bounded wait of this grid can record a code (a wait gives up only after 2 s,
+    // and CTA 0 is in the first wave).
+    if (p.small_n && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) p.status[0] = 0;
     // Work items: (chunk slot, v-head).  Without the short path the grid holds one CTA per item.
     // With it, how many slots the longer sequences own is known only on the device (the chunk
     // table's total), so a grid of at most two CTAs per SM takes items from a counter (status
     // word 2, zeroed by the chunk-table kernel), slot-major, until they run out.
     const bool persistent = p.short_path != 0;
-    const int items_valid = persistent ? p.chunk_base[p.N] * p.HV : 0;
+    // (the table's total can exceed the S workspace slots only for a cu_seqlens that is not
+    // non-decreasing; slots past S do not exist and are skipped)
+    const int items_valid = persistent ? min(p.chunk_base[p.N], p.S) * p.HV : 0;
     int* item_slot = reinterpret_cast<int*>(tslot + 1);
     uint32_t done = 0;  // chunks this CTA has processed: phase of every mbarrier
     int item = blockIdx.x;
@@ -176,7 +182,6 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                 if (lane == 0) {
                     s_lookup[0] = sq;
                     s_lookup[1] = cb;
-                    if (slot == 0 && hv == 0) atomicExch(p.status, 0);  // no table kernel ran this call
                 }
             }
             __syncthreads();

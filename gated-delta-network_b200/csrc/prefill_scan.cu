@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(288, 1)
     const int hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
+    // T == 0 with neither a chunk-table nor a prep launch: the scan is the call's only kernel
+    if (p.T == 0 && p.small_n && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) p.status[0] = 0;
     // CTA rows: the longest sequence first (N <= 32), so the critical path starts in the first
     // wave; with the short path, the compacted list of the longer sequences.
     const int row_i = blockIdx.y / p.HV;
@@ -109,7 +111,6 @@ __global__ void __launch_bounds__(288, 1)
         return;
     }
     if (p.short_path && len <= kShortLen) return;  // a short-sequence kernel owns it
-    const int nchunks = (len + kChunk - 1) / kChunk;
     int slot0;
     if (p.small_n) {
         int dummy;
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(288, 1)
     } else {
         slot0 = p.chunk_base[n];
     }
+    const int nchunks = clamp_chunks(p, slot0, (len + kChunk - 1) / kChunk, tid == 0);
 
     if (tid == 0) {
         for (int s = 0; s < C::kStages; ++s) {

@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait();  // the workspace comes from the prep kernel, the inputs from earlier work
     pdl_trigger();
+    // T == 0 with neither a chunk-table nor a prep launch: the scan is the call's only kernel
+    if (p.T == 0 && p.small_n && blockIdx.x == 0 && threadIdx.x == 0) p.status[0] = 0;
     if (blockIdx.x == 0) zero_unowned_tokens(p, tid, kThreads);
     // Work items: item = (row_i * HV + hv) * 2 + column half.  CTA rows are the longest sequence
     // first (N <= 32), or with the short path the compacted list of the longer sequences (as in
@@ -107,7 +109,7 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
         float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
         // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62);
         // with the short path a short-sequence kernel owns the sequences of up to kShortLen tokens
-        const int nchunks = (len <= 0 || (p.short_path && len <= kShortLen)) ? 0 : (len + kChunk - 1) / kChunk;
+        int nchunks = (len <= 0 || (p.short_path && len <= kShortLen)) ? 0 : (len + kChunk - 1) / kChunk;
         if (len <= 0)
             for (int idx = tid; idx < BV * kD; idx += kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
         int slot0 = 0;
@@ -118,6 +120,7 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
             } else {
                 slot0 = p.chunk_base[n];
             }
+            nchunks = clamp_chunks(p, slot0, nchunks, tid == 0);
         }
         if (nchunks > 0) {
             if (warp == kMath / 32) {
@@ -201,7 +204,7 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
                                       umma_desc_sw128(sbase + kOffHb + 2048u * kk, 8192, 1024), idesc_p, kk > 0);
                         umma_commit(bar_p);
                     }
-                    bool ok = mbar_wait(bar_p, g & 1u, p.status, kErrPrepMmaTimeout);
+                    bool ok = mbar_wait(bar_p, g & 1u, p.status, kErrScanMmaTimeout);
                     tc_fence_after();
                     GDN_PH_ACC(dbg, 21, tp);
                     {
@@ -299,7 +302,7 @@ __global__ void __launch_bounds__(tcs::kThreads, 1)
                         }
                     }
                     // an MMA_U that was not issued (a wait gave up) also fails this bounded wait
-                    if (ok) ok = mbar_wait(bar_u, g & 1u, p.status, kErrPrepMmaTimeout);
+                    if (ok) ok = mbar_wait(bar_u, g & 1u, p.status, kErrScanMmaTimeout);
                     tc_fence_after();
                     GDN_PH_ACC(dbg, 23, tp);
                     {

@@ -19,6 +19,8 @@ namespace gdn {
 constexpr int kErrScanTmaTimeout = 1;
 constexpr int kErrPrepTmaTimeout = 2;
 constexpr int kErrPrepMmaTimeout = 3;
+constexpr int kErrScanMmaTimeout = 4;
+constexpr int kErrBadSeqlens = 5;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {

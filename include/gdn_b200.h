@@ -29,12 +29,13 @@ extern "C" {
 enum gdn_status {
     GDN_OK = 0,
     GDN_ERR_NULL = 1,      /* a required pointer is NULL                          */
-    GDN_ERR_SHAPE = 2,     /* head counts / head size other than 4, 8, 128, 128    */
+    GDN_ERR_SHAPE = 2,     /* head size other than 128, or head counts outside the
+                              accepted family (see GDN_MAX_QK_HEADS)             */
     GDN_ERR_ALIGN = 3,     /* a pointer is not 16-byte aligned                     */
     GDN_ERR_SIZE = 4,      /* negative or inconsistent batch / token / seq counts  */
     GDN_ERR_WORKSPACE = 5, /* workspace missing, misaligned or too small           */
     GDN_ERR_CUDA = 6,      /* the CUDA runtime rejected the launch                 */
-    GDN_ERR_DEVICE = 7     /* current device is not sm_100 (B200)                 */
+    GDN_ERR_DEVICE = 7     /* current device is not compute capability 10.0 (B200) */
 };
 
 /* Flags (bitwise OR) accepted by the entry points.
@@ -60,6 +61,11 @@ enum gdn_status {
 #define GDN_DEVSTATUS_SCAN_TMA_TIMEOUT 1
 #define GDN_DEVSTATUS_PREP_TMA_TIMEOUT 2
 #define GDN_DEVSTATUS_PREP_MMA_TIMEOUT 3
+#define GDN_DEVSTATUS_SCAN_MMA_TIMEOUT 4
+/* cu_seqlens was not non-decreasing (overlapping or reversed sequences): the chunked kernels met
+ * more 64-token chunks than the workspace holds and skipped the excess (the outputs of such a call
+ * are invalid, but no access leaves the buffers). */
+#define GDN_DEVSTATUS_BAD_SEQLENS 5
 
 /* Fixed shape family (the reference asserts exactly these:
  * reference/gdn_decode_ref.py:32-36, reference/gdn_prefill_ref.py:33-36). */
@@ -154,7 +160,9 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
  * HV = 8; with more v-heads a call whose workspace would not fit also returns GDN_ERR_SIZE.
  * The call itself allocates nothing (no cudaMalloc / cudaFree).
  * The first call on each device (with that device current) looks up the array's device
- * address once; make that first call before any stream capture.
+ * address once; make that first call before any stream capture.  That cached address dies with
+ * the device's primary context: after cudaDeviceReset do not call this entry point on that device
+ * again in the same process.
  * All calls share the one array: calls that can overlap on the GPU (different streams,
  * or different host threads) race on it and must be serialised by the caller.  No part of
  * the array needs to start at zero: every location a call reads was written earlier in

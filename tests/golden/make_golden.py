@@ -4,7 +4,7 @@ Run in a container that has the reference sources (it imports the reference's
 own PyTorch oracles, reference/gdn_decode_ref.py::run and
 reference/gdn_prefill_ref.py::run, from REF_DIR) -- not needed on a GPU box:
 
-    python tests/golden/make_golden.py REF_DIR
+    python tests/golden/make_golden.py REF_DIR [CASE ...]   (no CASE: every fixture)
 
 Inputs are regenerated from seeds by tests/golden/inputs.py; each fixture
 stores a digest of its inputs (so a generator drift is detected), the full
@@ -44,6 +44,9 @@ PREFILL_CASES = [
     ("prefill_zero_len", dict(lens=[40, 0, 70], seed=20, with_state=True)),
     ("prefill_1", dict(lens=[1], seed=21, with_state=True)),
     ("prefill_200_state", dict(lens=[200], seed=22, with_state=True)),
+    # long sequences: pin the oracle's fp32 accumulation where the recurrence runs longest
+    ("prefill_2048_state", dict(lens=[2048], seed=23, with_state=True)),
+    ("prefill_1024x2_state", dict(lens=[1024, 1024], seed=24, with_state=True)),
 ]
 
 
@@ -60,12 +63,14 @@ def _summ(name, arr):
             f"{name}_shape": np.array(np.asarray(arr).shape, np.int64)}
 
 
-def main(ref_dir):
+def main(ref_dir, only=None):
     sys.path.insert(0, os.path.join(ref_dir, "reference"))
     from gdn_decode_ref import run as ref_decode  # the reference's own oracle
     from gdn_prefill_ref import run as ref_prefill
     torch.set_num_threads(os.cpu_count() or 1)
     for name, cfg in DECODE_CASES:
+        if only and name not in only:
+            continue
         inp = gi.decode_inputs(**cfg)
         st = None if inp["state"] is None else torch.from_numpy(inp["state"])
         out, ns = ref_decode(_bf16(inp["q"]), _bf16(inp["k"]), _bf16(inp["v"]), st, torch.from_numpy(inp["A_log"]),
@@ -76,6 +81,8 @@ def main(ref_dir):
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
         print("wrote", name)
     for name, cfg in PREFILL_CASES:
+        if only and name not in only:
+            continue
         inp = gi.prefill_inputs(**cfg)
         st = None if inp["state"] is None else torch.from_numpy(inp["state"])
         out, ns = ref_prefill(_bf16(inp["q"]), _bf16(inp["k"]), _bf16(inp["v"]), st, torch.from_numpy(inp["A_log"]),
@@ -89,6 +96,6 @@ def main(ref_dir):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py REF_DIR  (the reference checkout holding reference/gdn_*_ref.py)")
-    main(sys.argv[1])
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py REF_DIR [CASE ...]  (the reference checkout holding reference/gdn_*_ref.py)")
+    main(sys.argv[1], set(sys.argv[2:]) or None)

@@ -59,5 +59,5 @@ def test_prefill_qk16_v32_long_with_l2norm():
 
 def test_prefill_rejects_v_heads_not_multiple_of_8():
     inp = gi.prefill_inputs([10], seed=1, h=4, hv=12)
-    with pytest.raises(AssertionError):
+    with pytest.raises(ValueError):
         gdn.prefill.run(*util.prefill_args(inp))

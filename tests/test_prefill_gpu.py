@@ -408,3 +408,30 @@ def test_prefill_all_same_input_stays_finite(T, flags):
     else:
         assert np.abs(got - ref).max() <= 1e-2 * np.abs(ref).max()
         assert rel_state < 1e-2
+
+
+@pytest.mark.parametrize("scan", [16, 64], ids=["mma_sync_scan", "tcgen05_scan"])
+def test_prefill_overlapping_cu_seqlens_stays_in_bounds(scan):
+    """cu_seqlens that is not non-decreasing: sequence 3 = [128, 640) overlaps sequences 0 and 1, so
+    the sequences claim 16 chunks where the workspace holds 14 slots.  The kernels skip the excess
+    chunks, report GDN_DEVSTATUS_BAD_SEQLENS (5) and stay inside every buffer; sequence 0's slots
+    come first, so its final state is still that of sequence 0 alone."""
+    from gdn import prefill as pmod
+
+    T = 640
+    inp = gi.prefill_inputs([T], seed=35, with_state=True)
+    inp["state"] = np.concatenate([inp["state"]] * 4)
+    cu = torch.tensor([0, 256, 512, 128, 640], dtype=torch.int32, device="cuda")
+    args = list(util.prefill_args(inp))
+    args[8] = cu
+    out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(4, 8, 128, 128, dtype=torch.float32, device="cuda")
+    ws = torch.empty(gdn.prefill.workspace_bytes(4, T), dtype=torch.uint8, device="cuda")
+    pmod._launch(*args, out, ns, workspace=ws, flags=scan << 8)
+    torch.cuda.synchronize()
+    assert gdn.prefill.read_status(ws) == 5
+    one = dict(inp, state=inp["state"][:1], cu_seqlens=np.array([0, 256], np.int32))
+    for key in ("q", "k", "v", "a", "b"):
+        one[key] = inp[key][:256]
+    _, rs = _oracle(one)
+    util.check_state(ns[:1].cpu().numpy(), rs)

@@ -1,5 +1,5 @@
-"""Size-independent properties of the prefill path at the benchmark's full sizes, where the CPU
-oracle would take minutes: a sequence split at a chunk boundary and continued from the carried
+"""Full-size prefill checks: the BASELINE multi-GPU configuration (64 x 4096 tokens) against the
+CPU oracle, and size-independent properties at the benchmark's sizes: a sequence split at a chunk boundary and continued from the carried
 state gives the same outputs and final state as one call (the recurrence is the same one,
 reference/gdn_prefill_ref.py:56-89), and a packed batch gives, for every sequence, what the
 sequence gives alone (sequences are independent, reference/gdn_prefill_ref.py:56).  Inputs are
@@ -90,3 +90,20 @@ def test_prefill_packing_invariance_config3():
         torch.cuda.synchronize()
         _close(on, o[sl])
         _close(sn, s[n:n + 1])
+
+
+def test_prefill_config4_64x4096_matches_oracle():
+    """BASELINE config 4 at one GPU (64 sequences x 4096 tokens, per-sequence N(0, 0.02) initial
+    state; the persistent tcgen05 scan route) against the CPU oracle, at the path's bar: output
+    atol = rtol = 1e-2, final state rel-L2 1e-3.  The C oracle runs the 512 independent
+    (sequence, v-head) recurrences on all host cores in a few seconds."""
+    from oracle import oracle
+    from tests.golden import inputs as gi
+
+    inp = gi.prefill_inputs([4096] * 64, seed=64, with_state=True)
+    out, ns = gdn.prefill.run(*util.prefill_args(inp))
+    torch.cuda.synchronize()
+    ro, rs = oracle.prefill(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"],
+                            inp["b"], inp["cu_seqlens"], inp["scale"])
+    util.check_out(util.bits(out), ro)
+    util.check_state(ns.cpu().numpy(), rs)
