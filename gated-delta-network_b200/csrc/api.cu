@@ -164,6 +164,22 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     const unsigned forced_bv = (flags >> 8) & 0xffu;
     const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N, HV);
     if (bv != 8 && bv != 16 && bv != 32 && bv != 64) return GDN_ERR_SIZE;
+    // Segmented route: the default whenever the layout has its regions, unless a scan variant is
+    // forced or GDN_FLAG_NO_SEGMENTS is set; bits 16-23 force the segment length (it must not
+    // need more segment slots than the layout holds).
+    p.seg_m = (forced_bv || (flags & GDN_FLAG_NO_SEGMENTS)) ? 0 : lay.seg_m;
+    p.SS = lay.SS;
+    const unsigned forced_m = (flags >> 16) & 0xffu;
+    if (p.seg_m > 0 && forced_m) {
+        if ((long long)lay.S / forced_m + N > lay.SS && lay.S > lay.SS) return GDN_ERR_SIZE;
+        p.seg_m = (int)forced_m;
+    }
+    p.seg_D = reinterpret_cast<uint16_t*>(ws + lay.off_segD);
+    p.seg_B = reinterpret_cast<float*>(ws + lay.off_segB);
+    p.seg_gamma = reinterpret_cast<float*>(ws + lay.off_segG);
+    p.seg_hb = reinterpret_cast<uint16_t*>(ws + lay.off_seghb);
+    p.qpp = reinterpret_cast<uint16_t*>(ws + lay.off_qpp);
+    p.oipp = reinterpret_cast<uint16_t*>(ws + lay.off_oipp);
     if (gdn::launch_prefill(p, bv, static_cast<cudaStream_t>(stream)) != 0) return GDN_ERR_CUDA;
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }

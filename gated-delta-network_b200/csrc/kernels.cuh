@@ -63,12 +63,23 @@ struct PrefillArgs {
     uint16_t* qp;          // [8][S*64][128] bf16   Q' = diag(e^G) Q - Aqk w  (output operand)
     uint16_t* oi;          // [8][S][16][64][8] bf16 oi = Aqk u (intra-chunk output), column-group major
     float* g4;             // [8][S*64][4]   f32    {G, e^G, beta, rk} (rk = 1 / |k| with the L2 norm, else 1)
+    // Segmented route (seg_m > 0): each sequence's chunks are grouped into segments of seg_m
+    // chunks; a segment's transition h_end = gamma h_start + D h_start + B (prefill_seg.cu).
+    int seg_m;             // chunks per segment (0: the single-pass scan kernels)
+    int SS;                // segment slots in the workspace (>= sum over sequences of ceil(chunks / seg_m))
+    uint16_t* seg_D;       // [8][SS][128][128] bf16  D = transition - gamma I  (row = output k index)
+    float* seg_B;          // [8][SS][16][128][8] f32 B (state the segment builds from zero), column-group major
+    float* seg_gamma;      // [8][SS] f32           product of the segment's chunk decays
+    uint16_t* seg_hb;      // [8][SS][128 K][128 V] bf16  state at the segment start (output operand)
+    uint16_t* qpp;         // [8][S*64][128] bf16   Q'' = Q' Phi (Phi: transition from the segment start)
+    uint16_t* oipp;        // [8][S*64][128] bf16   oi'' = oi + Q' beta  (beta: state built from zero)
 };
 
 // Byte offsets of the workspace regions for N sequences and T tokens.
 struct PrefillLayout {
-    int S;
-    size_t off_status, off_base, off_seq, off_long, off_w, off_u, off_qp, off_oi, off_g4, total;
+    int S, SS, seg_m;
+    size_t off_status, off_base, off_seq, off_long, off_w, off_u, off_qp, off_oi, off_g4;
+    size_t off_segD, off_segB, off_segG, off_seghb, off_qpp, off_oipp, total;
 };
 
 // GDN_OK when the current device is compute capability 10.0 (B200), else a GDN_ERR_* code.
@@ -78,6 +89,21 @@ int launch_prefill(const PrefillArgs& p, int bv, cudaStream_t stream);
 // Slots: one per 64-token chunk of each sequence.  sum_n ceil(len_n / 64) <= T/64 + N, and
 // every chunk holds at least one token, so min(T/64 + N, T) slots always suffice.
 __host__ __device__ constexpr size_t prefill_up256(size_t x) { return (x + 255) & ~(size_t)255; }
+// Chunks per segment of the segmented route for a call of N sequences and T tokens, or 0 for
+// the single-pass scan.  A function of (N, T, HV) only, so the workspace size is known before
+// the call.  Few sequences of many chunks: the chain of one sequence is the critical path, and
+// splitting it into segments whose transitions are built in parallel shortens it.  The segment
+// length is the shortest that keeps the local-transition grid (two CTAs per segment and v-head)
+// within one wave of 148 SMs.
+__host__ __device__ constexpr int prefill_seg_m(int N, int T, int HV) {
+    if (N < 1 || N > 32 || HV < 1 || T < 512 * N) return 0;  // N <= kSmallN; >= 8 chunks per sequence on average
+    const long long nc = ((long long)T + 63) / 64;
+    for (int m = 2; m <= 64; ++m) {
+        const long long segs = (nc + m - 1) / m + (N - 1);  // bound on sum_n ceil(nc_n / m)
+        if (segs * 2 * HV <= 148) return m;
+    }
+    return 0;
+}
 __host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T, int HV = 8) {
     PrefillLayout L{};
     long long S = (long long)T / 64 + N;
@@ -104,6 +130,27 @@ __host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T, int HV 
     o = prefill_up256(o + (size_t)HV * rows * 128 * 2);
     L.off_g4 = o;
     o = prefill_up256(o + (size_t)HV * rows * 4 * 4);
+    L.seg_m = prefill_seg_m(N, T, HV);
+    L.SS = 0;
+    L.off_segD = L.off_segB = L.off_segG = L.off_seghb = L.off_qpp = L.off_oipp = o;
+    if (L.seg_m > 0) {
+        long long SS = (long long)S / L.seg_m + N;
+        if (SS > S) SS = S;
+        L.SS = (int)SS;
+        const size_t segs = (size_t)HV * (size_t)SS;
+        L.off_segD = o;
+        o = prefill_up256(o + segs * 128 * 128 * 2);
+        L.off_segB = o;
+        o = prefill_up256(o + segs * 128 * 128 * 4);
+        L.off_segG = o;
+        o = prefill_up256(o + segs * 4);
+        L.off_seghb = o;
+        o = prefill_up256(o + segs * 128 * 128 * 2);
+        L.off_qpp = o;
+        o = prefill_up256(o + (size_t)HV * rows * 128 * 2);
+        L.off_oipp = o;
+        o = prefill_up256(o + (size_t)HV * rows * 128 * 2);
+    }
     L.total = o;
     return L;
 }

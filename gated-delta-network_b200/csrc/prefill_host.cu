@@ -150,6 +150,13 @@ bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
     // Workspace: [8][R][cols] as (col, row, head); one box = one 64-row chunk slot.
     ok = ok && map3d(&m->w, p.w, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
     ok = ok && map3d(&m->qp, p.qp, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
+    if (p.seg_m > 0) {
+        const uint64_t RS = (uint64_t)p.SS * 128;
+        ok = ok && map3d(&m->qpp, p.qpp, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
+        ok = ok && map3d(&m->oipp, p.oipp, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
+        ok = ok && map3d(&m->segD, p.seg_D, BF, 128, RS, HV, 256, RS * 256, 64, 128, 1, SW);
+        ok = ok && map3d(&m->seghb, p.seg_hb, BF, 128, RS, HV, 256, RS * 256, 64, 128, 1, SW);
+    }
     return ok;
 }
 
@@ -186,7 +193,11 @@ int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
         PrefillMaps maps;
         if (!build_prefill_maps(p, &maps)) return -3;
         if (launch_prefill_prep(p, maps, stream) != 0) return -1;
-        if (launch_scan(p, maps, bv, stream) != 0) return -1;
+        if (p.seg_m > 0) {
+            if (launch_prefill_seg(p, maps, stream) != 0) return -1;
+        } else if (launch_scan(p, maps, bv, stream) != 0) {
+            return -1;
+        }
     } else {
         if (launch_scan(p, PrefillMaps{}, bv, stream) != 0) return -1;
     }

@@ -20,6 +20,11 @@ struct PrefillMaps {
     CUtensorMap b;    // same
     CUtensorMap w;    // (128 col, S*64 row, 8 head) bf16, box 64 x 64 x 1, SWIZZLE_128B
     CUtensorMap qp;   // (128, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B
+    // segmented route only
+    CUtensorMap qpp;  // Q''  (128, S*64, 8) bf16, box 64 x 64 x 1, SWIZZLE_128B
+    CUtensorMap oipp; // oi'' same
+    CUtensorMap segD; // D    (128, SS*128, 8) bf16, box 64 x 128 x 1, SWIZZLE_128B
+    CUtensorMap seghb;// h_s  (128, SS*128, 8) bf16, box 64 x 128 x 1, SWIZZLE_128B
 };
 
 // Sequence n's token range [s, e), clamped to [0, T] (malformed cu_seqlens cannot index outside).
@@ -124,6 +129,7 @@ __host__ __device__ __forceinline__ size_t cg_off(int hv, int S, int slot, int c
 int launch_prefill_prep(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cudaStream_t stream);
 int launch_prefill_scan_tc(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
+int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream);
 int launch_prefill_short(const PrefillArgs& p, cudaStream_t stream);
 int launch_prefill_short_rec(const PrefillArgs& p, cudaStream_t stream);
 

@@ -17,7 +17,7 @@ CSRC = os.path.join(os.path.dirname(PKG_DIR), "csrc")
 INCLUDE = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200.so")
-SOURCES = ["api.cu", "decode.cu", "prefill_host.cu", "prefill_prep.cu", "prefill_scan.cu", "prefill_scan_tc.cu", "prefill_short.cu", "prefill_short_rec.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "decode.cu", "prefill_host.cu", "prefill_prep.cu", "prefill_scan.cu", "prefill_scan_tc.cu", "prefill_short.cu", "prefill_short_rec.cu", "prefill_seg.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "kernels.cuh", "sm100.cuh", "prefill_kernels.cuh", "dbg.cuh"]
 
 NVCC_FLAGS = [

@@ -55,6 +55,11 @@ enum gdn_status {
  * norm of the reference's decode sweep kernel, tests/bench_decode_sweep.py:43-46, and of FLA's
  * use_qk_l2norm_in_kernel).  Without it q and k are used as given, as the reference oracles do. */
 #define GDN_FLAG_QK_L2NORM 0x4u
+/* Tuning: run the prefill's serial recurrence in one pass per sequence (no segments).  By default
+ * calls of few long sequences split every sequence into segments whose state transitions are
+ * built in parallel, then chained (gdn_prefill_fwd picks this from N and T).  Bits 16-23
+ * (value << 16) force the segment length in 64-token chunks for such calls. */
+#define GDN_FLAG_NO_SEGMENTS 0x8u
 
 /* Device-side status codes written to the first int of the prefill workspace. */
 #define GDN_DEVSTATUS_OK 0
