@@ -46,9 +46,10 @@ def test_workspace_bytes(lib):
     assert w1 % 256 == 0
     assert ws(16, 32768) > ws(1, 8192)
     assert lib.gdn_prefill_workspace_bytes(1, 1024, 4, 8, 64, 128) == 0  # unsupported shape
-    # other head counts: HV a multiple of H and of 8; the per-head regions scale with HV
+    # other head counts: HV a multiple of H and of 8; the per-head regions scale with HV (the
+    # segment regions of the segmented route also with the segment length, chosen per HV)
     ws32 = lib.gdn_prefill_workspace_bytes(1, 1024, 16, 32, 128, 128)
-    assert 3.5 * w1 < ws32 < 4.5 * w1
+    assert 2.5 * w1 < ws32 < 4.5 * w1
     assert lib.gdn_prefill_workspace_bytes(1, 1024, 4, 12, 128, 128) == 0
     assert lib.gdn_prefill_workspace_bytes(1, 1024, 3, 8, 128, 128) == 0
     assert lib.gdn_prefill_workspace_bytes(-1, 1024, 4, 8, 128, 128) == 0
