@@ -30,6 +30,9 @@
 
 #include "prefill_kernels.cuh"
 #include "sm100.cuh"
+#include "dbg.cuh"
+
+GDN_DBG_READER(gdn_debug_read_seg)
 
 namespace gdn {
 
@@ -201,14 +204,19 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
         constexpr uint32_t idesc_u = umma_idesc_bf16(128, 128, true, true);
         const CUtensorMap* omap = half ? &maps.qpp : &maps.oipp;
         float gamma = 1.f;
+        const bool dbg = true;
+        long long tp = clock64();
+        (void)dbg;
         int c = 0;
         for (; c < nch; ++c) {
             const uint32_t ph = (uint32_t)(c & 1);
             if (!mbar_wait(full + (c % kStages), (uint32_t)((c / kStages) & 1), p.status, kErrScanTmaTimeout))
                 *abort_flag = 1;
+            GDN_PH_ACC(dbg, 0, tp);
             fence_async_smem();  // this thread's X copy (generic stores) -> the tensor core
             tc_fence_before();
             named_bar_sync(1, kMath);
+            GDN_PH_ACC(dbg, 1, tp);
             if (*abort_flag) break;  // written only before this barrier
             tc_fence_after();
             const unsigned char* st = sm + (c % kStages) * kStage;
@@ -229,6 +237,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
             }
             bool ok = mbar_wait(bar_p, ph, p.status, kErrScanMmaTimeout);
             tc_fence_after();
+            GDN_PH_ACC(dbg, 2, tp);
             if (r < 64) {
                 // vn = ([u | 0] - W X) e^{G_L - G_r} / |k_r|  -> bf16 hi + lo, token row r
                 bool okv = true;
@@ -282,10 +291,12 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                     if (lane == 0) mbar_arrive(uo_empty);  // this warp's u rows are consumed
                 }
                 // warps 0, 1, 4, 5 alone gate MMA_U
+                GDN_PH_ACC(dbg, 3, tp);
                 fence_async_smem();
                 tc_fence_before();
                 okv = named_bar_and(2, 128, ok && okv);
                 tc_fence_after();
+                GDN_PH_ACC(dbg, 4, tp);
                 // MMA_U: K^T (128 x 64 tokens, MN-major) x (vn_hi + vn_lo) -> TMEM columns 128-255
                 if (okv && tid == 0) {
 #pragma unroll
@@ -348,8 +359,10 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                 ok = ok && oko;
             }
             // an MMA_U that was not issued (a wait gave up) also fails this bounded wait
+            GDN_PH_ACC(dbg, 5, tp);
             if (ok) ok = mbar_wait(bar_u, ph, p.status, kErrScanMmaTimeout);
             tc_fence_after();
+            GDN_PH_ACC(dbg, 6, tp);
             {
                 const float eL = __expf(GL);
 #pragma unroll
@@ -374,6 +387,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
             if (lane == 0) mbar_arrive(empty + (c % kStages));
             if (!ok) *abort_flag = 1;
             write_xb();
+            GDN_PH_ACC(dbg, 7, tp);
         }
         if (c < nch) {
             // gave up: let copies already in flight land (bounded) before the CTA exits
