@@ -23,8 +23,19 @@
 
 namespace {
 
-// Largest workspace any accepted call needs (the layout grows with both N and T).
-constexpr size_t kNoAllocBytes = gdn::prefill_layout(GDN_NOALLOC_MAX_SEQS, GDN_NOALLOC_MAX_TOKENS).total;
+// Largest workspace any accepted call needs (HV = 8).  The layout grows with N and T, and the
+// segmented route adds its regions for calls of few long sequences, so take the maximum over
+// every accepted (N, T).
+constexpr size_t noalloc_bytes() {
+    size_t m = 0;
+    for (int n = 0; n <= GDN_NOALLOC_MAX_SEQS; ++n)
+        for (int t = 0; t <= GDN_NOALLOC_MAX_TOKENS; ++t) {
+            const size_t b = gdn::prefill_layout(n, t).total;
+            if (b > m) m = b;
+        }
+    return m;
+}
+constexpr size_t kNoAllocBytes = noalloc_bytes();
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 

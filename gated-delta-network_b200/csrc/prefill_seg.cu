@@ -37,23 +37,24 @@ GDN_DBG_READER(gdn_debug_read_seg)
 namespace gdn {
 
 namespace segk {
-constexpr int kThreads = 288;  // 8 math warps (two per TMEM lane quarter) + 1 TMA producer warp
-constexpr int kMath = 256;
-constexpr int kStages = 2;
-constexpr uint32_t kOffWQ = 0;          // [W0 | Q'0 | W1 | Q'1], 8 KB each; after MMA_P: output staging
-constexpr uint32_t kOffK = 32768;       // k tile, 2 atoms of 64 tokens x 128 B
-constexpr uint32_t kOffG = 49152;       // [64][4] f32 {G, e^G, beta, rk}
-constexpr uint32_t kStage = 50176;      // 49 KB (1024-aligned)
-constexpr uint32_t kTxTiles = 6 * 8192 + 1024;
-constexpr uint32_t kOffU = kStages * kStage;   // u  f32 [16 cg][64][8] (half 0 only)
-constexpr uint32_t kOffOi = kOffU + 32768;     // oi bf16 [16 cg][64][8] (half 0 only)
-constexpr uint32_t kTxUO = 32768 + 16384;
-constexpr uint32_t kOffX = kOffOi + 16384;     // X bf16, 2 column blocks of [128 rows][128 B], SW128;
-                                               // between MMA_P and MMA_U: vn hi / lo [2][64][128 B] each
-constexpr uint32_t kOffBar = kOffX + 32768;    // full[2], empty[2], uo_full, uo_empty, mma_p, mma_u
-constexpr uint32_t kSmemUsed = kOffBar + 8 * 8 + 16;
+// One CTA per (segment, v-head): two groups of 8 math warps, group 0 carries beta (the state the
+// segment builds from zero, with u), group 1 Phi (the transition, without u).  The groups share
+// the chunk tiles and run independent chains, so one group's epilogues overlap the other's MMAs.
+constexpr int kGroupThreads = 256;
+constexpr int kThreads = 2 * kGroupThreads + 32;  // + 1 TMA producer warp
+constexpr uint32_t kOffWQ = 0;              // [W0 | Q'0 | W1 | Q'1], 8 KB each (single buffer)
+constexpr uint32_t kOffK = 32768;           // 2 stages of {k tile (2 atoms of 64 tokens x 128 B), G4 [64][4] f32}
+constexpr uint32_t kKStage = 17408;
+constexpr uint32_t kOffG = 16384;           // G4 inside a k stage
+constexpr uint32_t kOffU = kOffK + 2 * kKStage;   // u f32 [16 cg][64][8] (single buffer)
+constexpr uint32_t kOffX = kOffU + 32768;         // per group: X bf16, 2 column blocks of [128 rows][128 B],
+                                                  // SW128; between MMA_P and MMA_U: vn hi / lo [2][64][128 B]
+constexpr uint32_t kOffO = kOffX + 2 * 32768;     // per group: output tile bf16, 2 atoms of [64][128 B]
+constexpr uint32_t kOffBar = kOffO + 2 * 16384;   // wq_full, wq_empty, kfull[2], kempty[2], ufull, uempty,
+                                                  // bar_p[2], bar_u[2]
+constexpr uint32_t kSmemUsed = kOffBar + 8 * 12 + 16;
 constexpr uint32_t kSmem = kSmemUsed + 1024;
-constexpr uint32_t kTmemCols = 256;            // P: 0-127, D: 128-255
+constexpr uint32_t kTmemCols = 512;         // group g: P at 256 g, X at 256 g + 128
 static_assert(kSmem <= 227 * 1024, "segment kernel shared memory");
 }  // namespace segk
 
@@ -101,29 +102,32 @@ __device__ __forceinline__ SegSeq warp_seg_seq(const PrefillArgs& p, int kind, i
 // ------------------------------------------------------------------------------------------
 // 1. local transitions
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(segk::kThreads, 1)
+__global__ void __maxnreg__(120)
     gdn_prefill_seg_local_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace segk;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(sm);
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);
-    uint64_t* empty = full + kStages;
-    uint64_t* uo_full = empty + kStages;
-    uint64_t* uo_empty = uo_full + 1;
-    uint64_t* bar_p = uo_empty + 1;
-    uint64_t* bar_u = bar_p + 1;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_u + 1);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_u + 1) + 1;
+    uint64_t* wq_full = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* wq_empty = wq_full + 1;
+    uint64_t* kfull = wq_full + 2;
+    uint64_t* kempty = wq_full + 4;
+    uint64_t* ufull = wq_full + 6;
+    uint64_t* uempty = wq_full + 7;
+    uint64_t* bar_p = wq_full + 8;
+    uint64_t* bar_u = wq_full + 10;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(wq_full + 12);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ss = blockIdx.x, hv = blockIdx.y, half = blockIdx.z;  // half 0: beta (with u), 1: Phi
+    const int ss = blockIdx.x, hv = blockIdx.y;
     const int hq = hv / (p.HV / p.H);
-    if (warp == kMath / 32 && lane == 0) {
+    const int prod_warp = 2 * kGroupThreads / 32;
+    if (warp == prod_warp && lane == 0) {
         tma_prefetch_desc(&maps.w);
         tma_prefetch_desc(&maps.qp);
         tma_prefetch_desc(&maps.k);
-        tma_prefetch_desc(half ? &maps.qpp : &maps.oipp);
+        tma_prefetch_desc(&maps.qpp);
+        tma_prefetch_desc(&maps.oipp);
     }
     pdl_wait();  // the workspace comes from the prep kernel
     pdl_trigger();
@@ -131,23 +135,23 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
     if (sq.n < 0 || ss >= p.SS) return;  // a slot past the last segment (uniform across the CTA)
     int bos, eos;
     seq_bounds(p.cu, p.cu64, sq.n, p.T, bos, eos);
-    const int seg = ss - sq.sbase;
-    const int c0 = seg * p.seg_m;
+    const int c0 = (ss - sq.sbase) * p.seg_m;
     int nch = min(p.seg_m, sq.nc - c0);
     nch = max(0, min(nch, p.S - (sq.cbase + c0)));  // only a cu_seqlens that is not non-decreasing trims it
     if (nch <= 0) return;
     const int slot0 = sq.cbase + c0;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(full + s, 1);
-            mbar_init(empty + s, kMath / 32);
+        mbar_init(wq_full, 1);
+        mbar_init(wq_empty, 2);  // one arrival per group once its MMA_P has completed
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(kfull + s, 1);
+            mbar_init(kempty + s, 2);  // one arrival per group once its MMA_U has completed
+            mbar_init(bar_p + s, 1);
+            mbar_init(bar_u + s, 1);
         }
-        mbar_init(uo_full, 1);
-        mbar_init(uo_empty, kMath / 32);  // every math warp reads u (vn rows) or oi (output rows)
-        mbar_init(bar_p, 1);
-        mbar_init(bar_u, 1);
-        *abort_flag = 0;
+        mbar_init(ufull, 1);
+        mbar_init(uempty, 4);  // the four vn warps of group 0
         mbar_fence_init();
     }
     if (warp == 0) tmem_alloc(tslot, kTmemCols);
@@ -156,109 +160,137 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    if (warp == kMath / 32) {
-        // Producer: stage c % 2 gets chunk c's W, Q', K tiles and gates once chunk c - 2 is done;
-        // the single u / oi buffer (half 0) gets chunk c's u and oi once chunk c - 1 formed its vn.
+    if (warp == prod_warp) {
+        // Producer.  k stage c % 2 (k tile, gates) is refilled once both groups finished chunk c - 2;
+        // the single W / Q' buffer once both groups' MMA_P of chunk c - 1 completed; the single u
+        // buffer once group 0 formed chunk c - 1's vn.
         if (lane == 0) {
             for (int c = 0; c < nch; ++c) {
-                if (c >= kStages && !mbar_wait(empty + (c % kStages), (uint32_t)((c / kStages - 1) & 1), p.status,
-                                               kErrScanTmaTimeout))
-                    break;
-                unsigned char* st = sm + (c % kStages) * kStage;
-                uint64_t* bar = full + (c % kStages);
                 const int slot = slot0 + c, wr = slot * kChunk, t0 = bos + (c0 + c) * kChunk;
-                mbar_arrive_expect_tx(bar, kTxTiles);
-                tma_load_3d(st + kOffWQ, &maps.w, 0, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 8192, &maps.qp, 0, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 16384, &maps.w, 64, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 24576, &maps.qp, 64, wr, hv, bar);
-                tma_load_3d(st + kOffK, &maps.k, 0, hq, t0, bar);
-                tma_load_3d(st + kOffK + 8192, &maps.k, 64, hq, t0, bar);
-                bulk_load(st + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, bar);
-                if (half == 0) {
-                    if (c >= 1 && !mbar_wait(uo_empty, (uint32_t)((c - 1) & 1), p.status, kErrScanTmaTimeout)) break;
-                    mbar_arrive_expect_tx(uo_full, kTxUO);
-                    bulk_load(sm + kOffU, p.u + cg_off(hv, p.S, slot, 0), 32768, uo_full);
-                    bulk_load(sm + kOffOi, p.oi + cg_off(hv, p.S, slot, 0), 16384, uo_full);
-                }
+                if (c >= 2 && !mbar_wait(kempty + (c & 1), (uint32_t)(((c >> 1) - 1) & 1), p.status, kErrScanTmaTimeout))
+                    break;
+                unsigned char* ks = sm + kOffK + (c & 1) * kKStage;
+                mbar_arrive_expect_tx(kfull + (c & 1), 16384 + 1024);
+                tma_load_3d(ks, &maps.k, 0, hq, t0, kfull + (c & 1));
+                tma_load_3d(ks + 8192, &maps.k, 64, hq, t0, kfull + (c & 1));
+                bulk_load(ks + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, kfull + (c & 1));
+                if (c >= 1 && !mbar_wait(wq_empty, (uint32_t)((c - 1) & 1), p.status, kErrScanTmaTimeout)) break;
+                mbar_arrive_expect_tx(wq_full, 32768);
+                tma_load_3d(sm + kOffWQ, &maps.w, 0, wr, hv, wq_full);
+                tma_load_3d(sm + kOffWQ + 8192, &maps.qp, 0, wr, hv, wq_full);
+                tma_load_3d(sm + kOffWQ + 16384, &maps.w, 64, wr, hv, wq_full);
+                tma_load_3d(sm + kOffWQ + 24576, &maps.qp, 64, wr, hv, wq_full);
+                if (c >= 1 && !mbar_wait(uempty, (uint32_t)((c - 1) & 1), p.status, kErrScanTmaTimeout)) break;
+                mbar_arrive_expect_tx(ufull, 32768);
+                bulk_load(sm + kOffU, p.u + cg_off(hv, p.S, slot, 0), 32768, ufull);
             }
         }
     } else {
-        // ---- math warps: thread (r, hf) = TMEM lane r, state columns 64 hf .. 64 hf + 63 ----
-        const int r = lane + 32 * (warp & 3), hf = warp >> 2;
-        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * hf;
-        float x[64];  // X row r (K index), columns 64 hf + j
+        // ---- math: group g, thread (r, hf) = TMEM lane r, state columns 64 hf .. 64 hf + 63 ----
+        const int g = warp >> 3, gw = warp & 7;
+        const int r = lane + 32 * (gw & 3), hf = gw >> 2;
+        const int gt = tid - g * kGroupThreads;  // thread index inside the group
+        const uint32_t lanebits = (uint32_t)(32 * (gw & 3)) << 16;
+        const uint32_t tP = tmem + lanebits + 256u * g + 64u * hf;  // this thread's 64 P columns
+        const uint32_t tX = tP + 128u;                                // and 64 X columns
+        unsigned char* xb = sm + kOffX + g * 32768;
+        const uint32_t sxb = sbase + kOffX + (uint32_t)g * 32768u;
+        unsigned char* ob = sm + kOffO + g * 16384;
+        const CUtensorMap* omap = g ? &maps.qpp : &maps.oipp;
+        // X starts as 0 (beta) or I (Phi): in TMEM (fp32) and as the bf16 MMA operand
+        {
+            uint32_t z[32];
 #pragma unroll
-        for (int j = 0; j < 64; ++j) x[j] = (half == 1 && r == 64 * hf + j) ? 1.f : 0.f;
-        // bf16 copy of X: MN-major SW128 B operand of MMA_P, column block hf, row r
-        auto write_xb = [&]() {
-            unsigned char* row = sm + kOffX + hf * 16384 + r * 128;
+            for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj)
-                *reinterpret_cast<uint4*>(row + ((jj ^ (r & 7)) << 4)) =
-                    make_uint4(pack_bf16x2(x[8 * jj], x[8 * jj + 1]), pack_bf16x2(x[8 * jj + 2], x[8 * jj + 3]),
-                               pack_bf16x2(x[8 * jj + 4], x[8 * jj + 5]), pack_bf16x2(x[8 * jj + 6], x[8 * jj + 7]));
-        };
-        write_xb();
+                for (int j = 0; j < 32; ++j) z[j] = __float_as_uint((g == 1 && r == 64 * hf + 32 * blk + j) ? 1.f : 0.f);
+                tmem_st32(tX + 32u * blk, z);
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+                    *reinterpret_cast<uint4*>(xb + hf * 16384 + r * 128 + (((4 * blk + q4) ^ (r & 7)) << 4)) =
+                        make_uint4(pack_bf16x2(__uint_as_float(z[8 * q4]), __uint_as_float(z[8 * q4 + 1])),
+                                   pack_bf16x2(__uint_as_float(z[8 * q4 + 2]), __uint_as_float(z[8 * q4 + 3])),
+                                   pack_bf16x2(__uint_as_float(z[8 * q4 + 4]), __uint_as_float(z[8 * q4 + 5])),
+                                   pack_bf16x2(__uint_as_float(z[8 * q4 + 6]), __uint_as_float(z[8 * q4 + 7])));
+            }
+            tmem_st_wait();
+        }
         constexpr uint32_t idesc_p = umma_idesc_bf16(128, 128, false, true);
         constexpr uint32_t idesc_u = umma_idesc_bf16(128, 128, true, true);
-        const CUtensorMap* omap = half ? &maps.qpp : &maps.oipp;
-        float gamma = 1.f;
-        const bool dbg = true;
+        const bool dbg = g == 0;
         long long tp = clock64();
         (void)dbg;
+        float gamma = 1.f;
+        bool okc = true;  // every bounded wait of this thread so far succeeded
         int c = 0;
         for (; c < nch; ++c) {
             const uint32_t ph = (uint32_t)(c & 1);
-            if (!mbar_wait(full + (c % kStages), (uint32_t)((c / kStages) & 1), p.status, kErrScanTmaTimeout))
-                *abort_flag = 1;
+            bool ok = mbar_wait(kfull + (c & 1), (uint32_t)((c >> 1) & 1), p.status, kErrScanTmaTimeout) && okc;
+            ok = mbar_wait(wq_full, ph, p.status, kErrScanTmaTimeout) && ok;
             GDN_PH_ACC(dbg, 0, tp);
-            fence_async_smem();  // this thread's X copy (generic stores) -> the tensor core
+            if (gt == 128) tma_store_wait_read();  // the previous output tile has left the staging buffer
+            fence_async_smem();                     // X copy (generic stores) -> the tensor core
             tc_fence_before();
-            named_bar_sync(1, kMath);
-            GDN_PH_ACC(dbg, 1, tp);
-            if (*abort_flag) break;  // written only before this barrier
+            // a wait that gave up anywhere in the group stops the whole group (uniform break)
+            if (!named_bar_and(1 + g, kGroupThreads, ok)) break;
             tc_fence_after();
-            const unsigned char* st = sm + (c % kStages) * kStage;
-            const uint32_t sst = sbase + (uint32_t)(c % kStages) * kStage;
-            const float* G4 = reinterpret_cast<const float*>(st + kOffG);
+            GDN_PH_ACC(dbg, 1, tp);
+            const unsigned char* ks = sm + kOffK + (c & 1) * kKStage;
+            const uint32_t sks = sbase + kOffK + (uint32_t)(c & 1) * kKStage;
+            const float* G4 = reinterpret_cast<const float*>(ks + kOffG);
             const int slot = slot0 + c;
             const int t0 = bos + (c0 + c) * kChunk;
             const int L = min(kChunk, eos - t0);
             const float GL = G4[(L - 1) * 4];
-            // MMA_P: [W; Q'] (128 x 128, K-major) x X (128 x 128, MN-major) -> TMEM columns 0-127
-            if (tid == 0) {
+            const float eL = __expf(GL);
+            // MMA_P: [W; Q'] (128 x 128, K-major) x X (128 x 128, MN-major) -> P
+            if (gt == 0) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    umma_bf16(tmem,
-                              umma_desc_sw128(sst + kOffWQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
-                              umma_desc_sw128(sbase + kOffX + 2048u * kk, 16384, 1024), idesc_p, kk > 0);
-                umma_commit(bar_p);
+                    umma_bf16(tmem + 256u * g,
+                              umma_desc_sw128(sbase + kOffWQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+                              umma_desc_sw128(sxb + 2048u * kk, 16384, 1024), idesc_p, kk > 0);
+                umma_commit(bar_p + g);
             }
-            bool ok = mbar_wait(bar_p, ph, p.status, kErrScanMmaTimeout);
+            ok = mbar_wait(bar_p + g, ph, p.status, kErrScanMmaTimeout);
             tc_fence_after();
+            if (gt == 0) mbar_arrive(wq_empty);  // this group's MMA_P has read W / Q'
             GDN_PH_ACC(dbg, 2, tp);
+            // X <- e^{G_L} X in TMEM: MMA_U then accumulates K^T vn onto it
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                uint32_t d[32];
+                tmem_ld32_async(tX + 32u * blk, d);
+                tmem_ld_wait();
+                tmem_regs_ready(d);
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 v2 = mul2(make_float2(eL, eL), make_float2(__uint_as_float(d[j]), __uint_as_float(d[j + 1])));
+                    d[j] = __float_as_uint(v2.x);
+                    d[j + 1] = __float_as_uint(v2.y);
+                }
+                tmem_st32(tX + 32u * blk, d);
+            }
             if (r < 64) {
                 // vn = ([u | 0] - W X) e^{G_L - G_r} / |k_r|  -> bf16 hi + lo, token row r
-                bool okv = true;
-                if (half == 0) okv = mbar_wait(uo_full, ph, p.status, kErrScanTmaTimeout);
+                if (g == 0 && !mbar_wait(ufull, ph, p.status, kErrScanTmaTimeout)) ok = false;
                 const float4 g4r = *reinterpret_cast<const float4*>(G4 + r * 4);  // {G, e^G, beta, rk}
                 const float ed = __expf(GL - g4r.x) * g4r.w;
                 const float* Us = reinterpret_cast<const float*>(sm + kOffU);
-                unsigned char* rh = sm + kOffX + hf * 8192 + r * 128;
+                unsigned char* rh = xb + hf * 8192 + r * 128;
                 unsigned char* rl = rh + 16384;
                 const int hA = (r >> 2) & 1;
 #pragma unroll
                 for (int blk = 0; blk < 2; ++blk) {
                     uint32_t d[32];
-                    tmem_ld32_async(tl + 32u * blk, d);
+                    tmem_ld32_async(tP + 32u * blk, d);
                     tmem_ld_wait();
                     tmem_regs_ready(d);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int jj = 4 * blk + q4;  // 8-column group inside this thread's 64 columns
                         float uu[8];
-                        if (half == 0) {
+                        if (g == 0) {
                             const int cg = 8 * hf + jj;
                             const float4 x0 = *reinterpret_cast<const float4*>(Us + (cg * 64 + r) * 8 + 4 * hA);
                             const float4 x1 = *reinterpret_cast<const float4*>(Us + (cg * 64 + r) * 8 + 4 * (hA ^ 1));
@@ -286,139 +318,123 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                         *reinterpret_cast<uint4*>(rl + ((jj ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
                 }
-                if (half == 0) {
+                if (g == 0) {
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(uo_empty);  // this warp's u rows are consumed
+                    if (lane == 0) mbar_arrive(uempty);  // this warp's u rows are consumed
                 }
-                // warps 0, 1, 4, 5 alone gate MMA_U
-                GDN_PH_ACC(dbg, 3, tp);
-                fence_async_smem();
-                tc_fence_before();
-                okv = named_bar_and(2, 128, ok && okv);
-                tc_fence_after();
-                GDN_PH_ACC(dbg, 4, tp);
-                // MMA_U: K^T (128 x 64 tokens, MN-major) x (vn_hi + vn_lo) -> TMEM columns 128-255
-                if (okv && tid == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16(tmem + 128, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
-                                  umma_desc_sw128(sbase + kOffX + 2048u * kk, 8192, 1024), idesc_u, kk > 0);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16(tmem + 128, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
-                                  umma_desc_sw128(sbase + kOffX + 16384u + 2048u * kk, 8192, 1024), idesc_u, true);
-                    umma_commit(bar_u);
-                }
-                ok = okv;
             } else {
-                // output operand row m = r - 64: oi'' = oi + Q' beta (half 0) or Q'' = Q' Phi (half 1),
-                // staged SW128 in the stage's (consumed) W / Q' area, then one TMA store per 64 columns
+                // output operand row m = r - 64: oi'' = Q' beta (group 0) or Q'' = Q' Phi (group 1), bf16,
+                // staged SW128 for one TMA store per 64 columns
                 const int m = r - 64;
-                bool oko = true;
-                if (half == 0) oko = mbar_wait(uo_full, ph, p.status, kErrScanTmaTimeout);
-                const uint16_t* Os = reinterpret_cast<const uint16_t*>(sm + kOffOi);
-                unsigned char* orow = sm + (c % kStages) * kStage + kOffWQ + hf * 8192 + m * 128;
+                unsigned char* orow = ob + hf * 8192 + m * 128;
 #pragma unroll
                 for (int blk = 0; blk < 2; ++blk) {
                     uint32_t d[32];
-                    tmem_ld32_async(tl + 32u * blk, d);
+                    tmem_ld32_async(tP + 32u * blk, d);
                     tmem_ld_wait();
                     tmem_regs_ready(d);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int jj = 4 * blk + q4;
-                        uint32_t ow[4] = {0u, 0u, 0u, 0u};
-                        if (half == 0) {
-                            const uint4 oo = *reinterpret_cast<const uint4*>(Os + ((8 * hf + jj) * 64 + m) * 8);
-                            ow[0] = oo.x; ow[1] = oo.y; ow[2] = oo.z; ow[3] = oo.w;
-                        }
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 o2 = add2(make_float2(__uint_as_float(d[8 * q4 + 2 * e]),
-                                                               __uint_as_float(d[8 * q4 + 2 * e + 1])),
-                                                   make_float2(__uint_as_float(ow[e] << 16),
-                                                               __uint_as_float(ow[e] & 0xffff0000u)));
-                            pk[e] = pack_bf16x2(o2.x, o2.y);
-                        }
-                        *reinterpret_cast<uint4*>(orow + ((jj ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        *reinterpret_cast<uint4*>(orow + ((jj ^ (m & 7)) << 4)) =
+                            make_uint4(pack_bf16x2(__uint_as_float(d[8 * q4]), __uint_as_float(d[8 * q4 + 1])),
+                                       pack_bf16x2(__uint_as_float(d[8 * q4 + 2]), __uint_as_float(d[8 * q4 + 3])),
+                                       pack_bf16x2(__uint_as_float(d[8 * q4 + 4]), __uint_as_float(d[8 * q4 + 5])),
+                                       pack_bf16x2(__uint_as_float(d[8 * q4 + 6]), __uint_as_float(d[8 * q4 + 7])));
                     }
                 }
-                if (half == 0) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(uo_empty);  // this warp's oi rows are consumed
-                }
-                fence_async_smem();
-                named_bar_sync(3, 128);  // the four output warps
-                if (tid == 64) {         // warp 2, lane 0: store the 64 x 128 tile (two SW128 boxes)
-                    unsigned char* ob = sm + (c % kStages) * kStage + kOffWQ;
-                    tma_store_3d(omap, 0, slot * kChunk, hv, ob);
-                    tma_store_3d(omap, 64, slot * kChunk, hv, ob + 8192);
-                    tma_store_commit();
-                }
-                ok = ok && oko;
             }
-            // an MMA_U that was not issued (a wait gave up) also fails this bounded wait
-            GDN_PH_ACC(dbg, 5, tp);
-            if (ok) ok = mbar_wait(bar_u, ph, p.status, kErrScanMmaTimeout);
+            GDN_PH_ACC(dbg, 3, tp);
+            tmem_st_wait();      // the scaled X is in TMEM
+            fence_async_smem();  // vn and the output tile (generic stores) -> the tensor core / TMA
+            tc_fence_before();
+            ok = named_bar_and(1 + g, kGroupThreads, ok);
             tc_fence_after();
-            GDN_PH_ACC(dbg, 6, tp);
-            {
-                const float eL = __expf(GL);
+            GDN_PH_ACC(dbg, 4, tp);
+            // MMA_U: K^T (128 x 64 tokens, MN-major) x (vn_hi + vn_lo), accumulated onto X
+            if (ok && gt == 0) {
 #pragma unroll
-                for (int blk = 0; blk < 2; ++blk) {
-                    uint32_t d[32];
-                    tmem_ld32_async(tl + 128u + 32u * blk, d);
-                    tmem_ld_wait();
-                    tmem_regs_ready(d);
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(tmem + 256u * g + 128u, umma_desc_sw128(sks + 2048u * kk, 8192, 1024),
+                              umma_desc_sw128(sxb + 2048u * kk, 8192, 1024), idesc_u, true);
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        const float2 xn = fma2(make_float2(eL, eL), make_float2(x[32 * blk + j], x[32 * blk + j + 1]),
-                                               make_float2(__uint_as_float(d[j]), __uint_as_float(d[j + 1])));
-                        x[32 * blk + j] = xn.x;
-                        x[32 * blk + j + 1] = xn.y;
-                    }
-                }
-                gamma *= eL;
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(tmem + 256u * g + 128u, umma_desc_sw128(sks + 2048u * kk, 8192, 1024),
+                              umma_desc_sw128(sxb + 16384u + 2048u * kk, 8192, 1024), idesc_u, true);
+                umma_commit(bar_u + g);
             }
-            // the stage's operands are consumed (and its output tile read by the TMA store)
-            if (tid == 64) tma_store_wait_read();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty + (c % kStages));
-            if (!ok) *abort_flag = 1;
-            write_xb();
+            if (gt == 128) {  // the output tile: two SW128 boxes of 64 columns
+                tma_store_3d(omap, 0, slot * kChunk, hv, ob);
+                tma_store_3d(omap, 64, slot * kChunk, hv, ob + 8192);
+                tma_store_commit();
+            }
+            GDN_PH_ACC(dbg, 5, tp);
+            // an MMA_U that was not issued (a wait gave up) also fails this bounded wait
+            if (ok) ok = mbar_wait(bar_u + g, ph, p.status, kErrScanMmaTimeout);
+            tc_fence_after();
+            if (gt == 0) mbar_arrive(kempty + (c & 1));  // this group is done with the k tile and gates
+            GDN_PH_ACC(dbg, 6, tp);
+            // bf16 copy of the new X for the next MMA_P
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                uint32_t d[32];
+                tmem_ld32_async(tX + 32u * blk, d);
+                tmem_ld_wait();
+                tmem_regs_ready(d);
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+                    *reinterpret_cast<uint4*>(xb + hf * 16384 + r * 128 + (((4 * blk + q4) ^ (r & 7)) << 4)) =
+                        make_uint4(pack_bf16x2(__uint_as_float(d[8 * q4]), __uint_as_float(d[8 * q4 + 1])),
+                                   pack_bf16x2(__uint_as_float(d[8 * q4 + 2]), __uint_as_float(d[8 * q4 + 3])),
+                                   pack_bf16x2(__uint_as_float(d[8 * q4 + 4]), __uint_as_float(d[8 * q4 + 5])),
+                                   pack_bf16x2(__uint_as_float(d[8 * q4 + 6]), __uint_as_float(d[8 * q4 + 7])));
+            }
+            gamma *= eL;
+            okc = ok;
             GDN_PH_ACC(dbg, 7, tp);
         }
         if (c < nch) {
             // gave up: let copies already in flight land (bounded) before the CTA exits
-            if (tid == 0)
-                for (int cc = c + 1; cc < min(nch, c + kStages); ++cc)
-                    mbar_wait(full + (cc % kStages), (uint32_t)((cc / kStages) & 1), nullptr, 0);
-        } else {
-            const size_t seg_i = (size_t)hv * p.SS + ss;
-            if (half == 0) {
-                // B = beta_end, column-group major [16][128][8] f32
-                float* Bp = p.seg_B + seg_i * 128 * 128;
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    float4* dst = reinterpret_cast<float4*>(Bp + ((8 * hf + jj) * 128 + r) * 8);
-                    dst[0] = make_float4(x[8 * jj], x[8 * jj + 1], x[8 * jj + 2], x[8 * jj + 3]);
-                    dst[1] = make_float4(x[8 * jj + 4], x[8 * jj + 5], x[8 * jj + 6], x[8 * jj + 7]);
-                }
-            } else {
-                // D = Phi_end - gamma I, row-major [128][128] bf16 (row = output k index)
-#pragma unroll
-                for (int j = 0; j < 64; ++j)
-                    if (r == 64 * hf + j) x[j] -= gamma;
-                uint4* dst = reinterpret_cast<uint4*>(p.seg_D + (seg_i * 128 + r) * 128 + 64 * hf);
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj)
-                    dst[jj] = make_uint4(pack_bf16x2(x[8 * jj], x[8 * jj + 1]), pack_bf16x2(x[8 * jj + 2], x[8 * jj + 3]),
-                                         pack_bf16x2(x[8 * jj + 4], x[8 * jj + 5]), pack_bf16x2(x[8 * jj + 6], x[8 * jj + 7]));
-                if (tid == 0) p.seg_gamma[seg_i] = gamma;
+            if (gt == 0) {
+                for (int cc = c; cc < min(nch, c + 2); ++cc)
+                    mbar_wait(kfull + (cc & 1), (uint32_t)((cc >> 1) & 1), nullptr, 0);
+                mbar_wait(wq_full, (uint32_t)(c & 1), nullptr, 0);
+                if (g == 0) mbar_wait(ufull, (uint32_t)(c & 1), nullptr, 0);
             }
+        } else {
+            // segment transition: B = beta_end (group 0), D = Phi_end - gamma I and gamma (group 1)
+            const size_t seg_i = (size_t)hv * p.SS + ss;
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                uint32_t d[32];
+                tmem_ld32_async(tX + 32u * blk, d);
+                tmem_ld_wait();
+                tmem_regs_ready(d);
+                if (g == 0) {
+                    float* Bp = p.seg_B + seg_i * 128 * 128;  // column-group major [16][128][8] f32
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float4* dst = reinterpret_cast<float4*>(Bp + ((8 * hf + 4 * blk + q4) * 128 + r) * 8);
+                        dst[0] = make_float4(__uint_as_float(d[8 * q4]), __uint_as_float(d[8 * q4 + 1]),
+                                             __uint_as_float(d[8 * q4 + 2]), __uint_as_float(d[8 * q4 + 3]));
+                        dst[1] = make_float4(__uint_as_float(d[8 * q4 + 4]), __uint_as_float(d[8 * q4 + 5]),
+                                             __uint_as_float(d[8 * q4 + 6]), __uint_as_float(d[8 * q4 + 7]));
+                    }
+                } else {
+                    float x[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        x[j] = __uint_as_float(d[j]) - ((r == 64 * hf + 32 * blk + j) ? gamma : 0.f);
+                    uint4* dst = reinterpret_cast<uint4*>(p.seg_D + (seg_i * 128 + r) * 128 + 64 * hf + 32 * blk);
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4)
+                        dst[q4] = make_uint4(pack_bf16x2(x[8 * q4], x[8 * q4 + 1]), pack_bf16x2(x[8 * q4 + 2], x[8 * q4 + 3]),
+                                             pack_bf16x2(x[8 * q4 + 4], x[8 * q4 + 5]), pack_bf16x2(x[8 * q4 + 6], x[8 * q4 + 7]));
+                }
+            }
+            if (g == 1 && gt == 0) p.seg_gamma[seg_i] = gamma;
         }
-        if (tid == 64) tma_store_wait_all();  // the operand stores are complete before the grid ends
+        if (gt == 128) tma_store_wait_all();  // the operand stores are complete before the grid ends
     }
     tc_fence_before();
     __syncthreads();
@@ -619,6 +635,8 @@ __global__ void __launch_bounds__(sego::kThreads)
         if (tid == 0) mbar_wait(bar, 0, nullptr, 0);
         return;
     }
+    // oi = Aqk u of the chunk (prep kernel, column-group major [16][64][8] bf16)
+    const uint16_t* oi_slot = p.oi + cg_off(hv, p.S, slot, 0);
     // warp w: output rows 16 (w & 3) .. +15, columns 64 (w >> 2) .. +63
     const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
     float acc[8][4];
@@ -649,9 +667,11 @@ __global__ void __launch_bounds__(sego::kThreads)
         for (int nt = 0; nt < 8; ++nt) {
             const int col = n0 + 8 * nt + 2 * tq;
             const uint32_t oo = *reinterpret_cast<const uint32_t*>(sm + kOffO + sw128_off(row, col, 8192));
-            *reinterpret_cast<uint32_t*>(dst + col) =
-                pack_bf16x2(p.scale * (acc[nt][2 * hh] + __uint_as_float(oo << 16)),
-                            p.scale * (acc[nt][2 * hh + 1] + __uint_as_float(oo & 0xffff0000u)));
+            const uint32_t oc = *reinterpret_cast<const uint32_t*>(oi_slot + (col >> 3) * 512 + row * 8 + (col & 7));
+            const float2 o2 = add2(add2(make_float2(acc[nt][2 * hh], acc[nt][2 * hh + 1]),
+                                        make_float2(__uint_as_float(oo << 16), __uint_as_float(oo & 0xffff0000u))),
+                                   make_float2(__uint_as_float(oc << 16), __uint_as_float(oc & 0xffff0000u)));
+            *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16x2(p.scale * o2.x, p.scale * o2.y);
         }
     }
 }
@@ -666,7 +686,7 @@ int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream
         return -1;
     // segment slots actually used: sum_n ceil(nc_n / m) <= min(SS, ceil(T / 64 / m) + N - 1)
     const long long segs = std::min<long long>(p.SS, ((long long)p.T + 64LL * p.seg_m - 1) / (64LL * p.seg_m) + p.N - 1);
-    if (launch_pdl(gdn_prefill_seg_local_kernel, dim3((unsigned)std::max<long long>(segs, 1), p.HV, 2),
+    if (launch_pdl(gdn_prefill_seg_local_kernel, dim3((unsigned)std::max<long long>(segs, 1), p.HV),
                    dim3(segk::kThreads), segk::kSmem, stream, p, maps) != cudaSuccess)
         return -1;
     if (launch_pdl(gdn_prefill_seg_chain_kernel, dim3(kD / segc::BV, p.N, p.HV), dim3(segc::kThreads), segc::kSmem,

@@ -159,7 +159,7 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
  *
  * Same arguments and results as gdn_prefill_fwd minus `workspace` / `workspace_bytes`: the
  * workspace is a fixed device array inside the library, sized for GDN_NOALLOC_MAX_TOKENS
- * packed tokens in at most GDN_NOALLOC_MAX_SEQS sequences (about 22 MB), which every GPU
+ * packed tokens in at most GDN_NOALLOC_MAX_SEQS sequences (about 42 MB), which every GPU
  * that loads the library holds until the process exits.  T > GDN_NOALLOC_MAX_TOKENS or
  * N > GDN_NOALLOC_MAX_SEQS returns GDN_ERR_SIZE and launches nothing.  The array is sized for
  * HV = 8; with more v-heads a call whose workspace would not fit also returns GDN_ERR_SIZE.

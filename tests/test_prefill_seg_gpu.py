@@ -55,9 +55,11 @@ def test_segmented_prefill_matches_oracle(lens, with_state):
     util.check_state(ns.cpu().numpy(), ns1.cpu().numpy())
 
 
-@pytest.mark.parametrize("m", [2, 3, 8, 31, 64, 128])
+@pytest.mark.parametrize("m", [8, 11, 31, 64, 128])
 def test_segmented_prefill_forced_segment_lengths(m):
-    """Segment lengths from 2 chunks to the whole sequence (one segment) give the oracle's results."""
+    """Segment lengths from the default (8 chunks at 4096 tokens) up to the whole sequence (one
+    segment) give the oracle's results.  Shorter ones would need more segment slots than the
+    workspace holds (GDN_ERR_SIZE, checked below)."""
     inp = gi.prefill_inputs([4096], seed=77, with_state=True)
     out, ns = _call(inp, m << 16)
     ro, rs = _oracle(inp)
@@ -107,3 +109,10 @@ def test_segmented_prefill_in_place_and_graph_capture():
     torch.cuda.synchronize()
     util.check_out(util.bits(out), ro)
     util.check_state(st.cpu().numpy(), rs)
+
+
+def test_segmented_prefill_rejects_segments_beyond_the_workspace():
+    inp = gi.prefill_inputs([4096], seed=80, with_state=True)
+    with pytest.raises(gdn.GDNError) as e:
+        _call(inp, 2 << 16)
+    assert e.value.status == 4  # GDN_ERR_SIZE
