@@ -43,3 +43,30 @@ def seq_shard(cu_seqlens: Sequence[int], world: int, rank: int):
     t0, t1 = cu[s0], cu[s1]
     local = [x - t0 for x in cu[s0:s1 + 1]]
     return s0, s1, t0, t1, local
+
+
+def head_shard(num_qk_heads: int, num_v_heads: int, world: int, rank: int, prefill: bool = False):
+    """Split the heads of a call over ranks, for calls with fewer independent sequences (or batch
+    elements) than ranks.  Each q/k head and the v-heads that read it (v-head hv reads q/k head
+    hv // (HV // H)) stay on one rank, so the shards exchange nothing.
+
+    Returns (qk_start, qk_stop, v_start, v_stop): the rank's q/k heads and v-heads.  The rank
+    runs the path on q[..., qk_start:qk_stop, :], k likewise, and v, a, b, A_log, dt_bias and the
+    state sliced to [v_start, v_stop) along their head dimension.
+
+    The split needs world to divide the number of q/k heads.  Prefill kernels read the gates in
+    8-head tiles, so with prefill=True each rank must also keep a multiple of 8 v-heads (e.g. the
+    32-v-head family over up to 4 ranks); a split that cannot satisfy these raises ValueError.
+    """
+    H, HV = int(num_qk_heads), int(num_v_heads)
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("need world > 0 and 0 <= rank < world")
+    if H <= 0 or HV % H:
+        raise ValueError(f"v-heads ({HV}) must be a multiple of q/k heads ({H})")
+    if H % world:
+        raise ValueError(f"{world} ranks cannot split {H} q/k heads into equal groups")
+    hq = H // world
+    hv = HV // world
+    if prefill and hv % 8:
+        raise ValueError(f"prefill needs a multiple of 8 v-heads per rank (got {hv})")
+    return rank * hq, (rank + 1) * hq, rank * hv, (rank + 1) * hv

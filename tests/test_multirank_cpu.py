@@ -9,7 +9,7 @@ import pytest
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from gdn.shard import batch_shard, seq_shard
+from gdn.shard import batch_shard, head_shard, seq_shard
 
 
 def test_batch_shard_covers_everything():
@@ -31,6 +31,20 @@ def test_seq_shard_rebases_and_covers():
         ps = [seq_shard(cu2, world, r) for r in range(world)]
         assert ps[0][0] == 0 and ps[-1][1] == 5
         assert all(ps[i][1] == ps[i + 1][0] for i in range(world - 1))
+
+
+def test_head_shard_groups_and_constraints():
+    # decode, the reference family (4 q/k heads, 8 v-heads): 1, 2 or 4 ranks
+    for world in (1, 2, 4):
+        parts = [head_shard(4, 8, world, r) for r in range(world)]
+        assert parts[0][0] == 0 and parts[-1][1] == 4 and parts[0][2] == 0 and parts[-1][3] == 8
+        for a0, a1, b0, b1 in parts:
+            assert b0 == a0 * 2 and b1 == a1 * 2  # each v-head stays with the q/k head it reads
+    with pytest.raises(ValueError):
+        head_shard(4, 8, 3, 0)  # 3 does not divide 4 q/k heads
+    with pytest.raises(ValueError):
+        head_shard(4, 8, 2, 0, prefill=True)  # 4 v-heads per rank: below the 8-head gate tiles
+    assert head_shard(16, 32, 4, 3, prefill=True) == (12, 16, 24, 32)
 
 
 def _free_port():
@@ -65,10 +79,24 @@ def _worker(rank, world, port, q):
                                 p["a"][t0:t1], p["dt_bias"], p["b"][t0:t1], np.array(lcu), p["scale"], threads=1)
         pre = [None] * world
         dist.all_gather_object(pre, (po, ps))
+        # one sequence split by v-head groups (fewer sequences than ranks): decode of the reference
+        # family (4 q/k heads, 8 v-heads) and prefill of the 16 / 32 family
+        h0, h1, v0, v1 = head_shard(4, 8, world, rank)
+        hd = gi.decode_inputs(1, seed=5)
+        ho = oracle.decode(hd["q"][:, :, h0:h1], hd["k"][:, :, h0:h1], hd["v"][:, :, v0:v1], hd["state"][:, v0:v1],
+                           hd["A_log"][v0:v1], hd["a"][:, :, v0:v1], hd["dt_bias"][v0:v1], hd["b"][:, :, v0:v1],
+                           hd["scale"], threads=1)
+        hp = gi.prefill_inputs([150], seed=6, h=16, hv=32)
+        h0, h1, v0, v1 = head_shard(16, 32, world, rank, prefill=True)
+        hpo = oracle.prefill(hp["q"][:, h0:h1], hp["k"][:, h0:h1], hp["v"][:, v0:v1], hp["state"][:, v0:v1],
+                             hp["A_log"][v0:v1], hp["a"][:, v0:v1], hp["dt_bias"][v0:v1], hp["b"][:, v0:v1],
+                             hp["cu_seqlens"], hp["scale"], threads=1)
+        heads = [None] * world
+        dist.all_gather_object(heads, (ho, hpo))
         t = torch.tensor([float(rank + 1)], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         if rank == 0:
-            q.put((dec, pre, float(t.item())))
+            q.put((dec, pre, heads, float(t.item())))
     finally:
         dist.destroy_process_group()
 
@@ -85,7 +113,7 @@ def test_two_rank_sharded_oracle_matches_single_process():
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    dec, pre, tmax = q.get()
+    dec, pre, heads, tmax = q.get()
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -99,3 +127,14 @@ def test_two_rank_sharded_oracle_matches_single_process():
                             p["cu_seqlens"], p["scale"])
     assert np.array_equal(np.concatenate([x[0] for x in pre]), po)
     assert np.array_equal(np.concatenate([x[1] for x in pre]), ps)
+
+    hd = gi.decode_inputs(1, seed=5)
+    fo, fs = oracle.decode(hd["q"], hd["k"], hd["v"], hd["state"], hd["A_log"], hd["a"], hd["dt_bias"], hd["b"],
+                           hd["scale"])
+    assert np.array_equal(np.concatenate([x[0][0] for x in heads], axis=2), fo)
+    assert np.array_equal(np.concatenate([x[0][1] for x in heads], axis=1), fs)
+    hp = gi.prefill_inputs([150], seed=6, h=16, hv=32)
+    po, ps = oracle.prefill(hp["q"], hp["k"], hp["v"], hp["state"], hp["A_log"], hp["a"], hp["dt_bias"], hp["b"],
+                            hp["cu_seqlens"], hp["scale"])
+    assert np.array_equal(np.concatenate([x[1][0] for x in heads], axis=1), po)
+    assert np.array_equal(np.concatenate([x[1][1] for x in heads], axis=1), ps)
