@@ -102,7 +102,7 @@ __device__ __forceinline__ SegSeq warp_seg_seq(const PrefillArgs& p, int kind, i
 // ------------------------------------------------------------------------------------------
 // 1. local transitions
 // ------------------------------------------------------------------------------------------
-__global__ void __maxnreg__(120)
+__global__ void __maxnreg__(112)
     gdn_prefill_seg_local_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace segk;
     extern __shared__ unsigned char smem_raw[];
