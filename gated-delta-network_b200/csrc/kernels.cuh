@@ -93,14 +93,14 @@ __host__ __device__ constexpr size_t prefill_up256(size_t x) { return (x + 255) 
 // the single-pass scan.  A function of (N, T, HV) only, so the workspace size is known before
 // the call.  Few sequences of many chunks: the chain of one sequence is the critical path, and
 // splitting it into segments whose transitions are built in parallel shortens it.  The segment
-// length is the shortest that keeps the local-transition grid (one CTA per segment and v-head)
+// length is the shortest that keeps the local-transition grid (two CTAs per segment and v-head)
 // within one wave of 148 SMs.
 __host__ __device__ constexpr int prefill_seg_m(int N, int T, int HV) {
     if (N < 1 || N > 32 || HV < 1 || T < 512 * N) return 0;  // N <= kSmallN; >= 8 chunks per sequence on average
     const long long nc = ((long long)T + 63) / 64;
     for (int m = 2; m <= 64; ++m) {
         const long long segs = (nc + m - 1) / m + (N - 1);  // bound on sum_n ceil(nc_n / m)
-        if (segs * HV <= 148) return m;
+        if (segs * 2 * HV <= 148) return m;
     }
     return 0;
 }

@@ -13,13 +13,14 @@
 //      product of the chunk transitions so far).  Per chunk j it also forms the output operands
 //      of every chunk against the segment's start state h_s:
 //          o_j = scale (Q'_j h_j + oi_j),  h_j = Phi_j h_s + beta_j
-//              = scale (Q''_j h_s + oi''_j),  Q''_j = Q'_j Phi_j,  oi''_j = oi_j + Q'_j beta_j.
+//              = scale (Q''_j h_s + oi''_j + oi_j),  Q''_j = Q'_j Phi_j,  oi''_j = Q'_j beta_j.
 //      At the end it stores the segment transition h_{s+1} = gamma h_s + D h_s + B with
 //      B = beta_end, gamma = product of e^{G_L}, D = Phi_end - gamma I.
 //   2. gdn_prefill_seg_chain_kernel, one CTA per (8 state columns, sequence, v-head): the short
 //      serial chain over segments, h_{s+1} = gamma h_s + D h_s + B; it records each h_s (bf16,
 //      the output operand) and writes the final state.
-//   3. gdn_prefill_seg_out_kernel, one CTA per (chunk, v-head): o_j = scale (Q''_j h_s + oi''_j).
+//   3. gdn_prefill_seg_out_kernel, one CTA per (4 chunks of a segment, v-head):
+//      o_j = scale (Q''_j h_s + oi''_j + oi_j), oi_j = Aqk u from the prep.
 //
 // Per chunk the local kernel does what the single-pass scan does (two dependent products), on a
 // state twice as wide, but every segment runs at once: the serial work per sequence drops from
@@ -37,24 +38,21 @@ GDN_DBG_READER(gdn_debug_read_seg)
 namespace gdn {
 
 namespace segk {
-// One CTA per (segment, v-head): two groups of 8 math warps, group 0 carries beta (the state the
-// segment builds from zero, with u), group 1 Phi (the transition, without u).  The groups share
-// the chunk tiles and run independent chains, so one group's epilogues overlap the other's MMAs.
-constexpr int kGroupThreads = 256;
-constexpr int kThreads = 2 * kGroupThreads + 32;  // + 1 TMA producer warp
-constexpr uint32_t kOffWQ = 0;              // [W0 | Q'0 | W1 | Q'1], 8 KB each (single buffer)
-constexpr uint32_t kOffK = 32768;           // 2 stages of {k tile (2 atoms of 64 tokens x 128 B), G4 [64][4] f32}
-constexpr uint32_t kKStage = 17408;
-constexpr uint32_t kOffG = 16384;           // G4 inside a k stage
-constexpr uint32_t kOffU = kOffK + 2 * kKStage;   // u f32 [16 cg][64][8] (single buffer)
-constexpr uint32_t kOffX = kOffU + 32768;         // per group: X bf16, 2 column blocks of [128 rows][128 B],
-                                                  // SW128; between MMA_P and MMA_U: vn hi / lo [2][64][128 B]
-constexpr uint32_t kOffO = kOffX + 2 * 32768;     // per group: output tile bf16, 2 atoms of [64][128 B]
-constexpr uint32_t kOffBar = kOffO + 2 * 16384;   // wq_full, wq_empty, kfull[2], kempty[2], ufull, uempty,
-                                                  // bar_p[2], bar_u[2]
-constexpr uint32_t kSmemUsed = kOffBar + 8 * 12 + 16;
+constexpr int kThreads = 288;  // 8 math warps (two per TMEM lane quarter) + 1 TMA producer warp
+constexpr int kMath = 256;
+constexpr int kStages = 2;
+constexpr uint32_t kOffWQ = 0;          // [W0 | Q'0 | W1 | Q'1], 8 KB each; after MMA_P: output staging
+constexpr uint32_t kOffK = 32768;       // k tile, 2 atoms of 64 tokens x 128 B
+constexpr uint32_t kOffG = 49152;       // [64][4] f32 {G, e^G, beta, rk}
+constexpr uint32_t kOffU = 50176;       // u f32 [16 cg][64][8] (half 0 only)
+constexpr uint32_t kStage = 82944;      // 81 KB (1024-aligned)
+constexpr uint32_t kTxTiles = 6 * 8192 + 1024;
+constexpr uint32_t kOffX = kStages * kStage;   // X bf16, 2 column blocks of [128 rows][128 B], SW128;
+                                               // between MMA_P and MMA_U: vn hi / lo [2][64][128 B] each
+constexpr uint32_t kOffBar = kOffX + 32768;    // full[2], empty[2], mma_p, mma_u
+constexpr uint32_t kSmemUsed = kOffBar + 8 * 6 + 16;
 constexpr uint32_t kSmem = kSmemUsed + 1024;
-constexpr uint32_t kTmemCols = 512;         // group g: P at 256 g, X at 256 g + 128
+constexpr uint32_t kTmemCols = 256;            // P: 0-127, D: 128-255
 static_assert(kSmem <= 227 * 1024, "segment kernel shared memory");
 }  // namespace segk
 
@@ -99,35 +97,42 @@ __device__ __forceinline__ SegSeq warp_seg_seq(const PrefillArgs& p, int kind, i
     return r;
 }
 
+// bf16 copy of X row r, columns 64 hf .. +63: MN-major SW128 B operand of MMA_P, column block hf
+#define GDN_SEG_WRITE_XB()                                                                                     \
+    do {                                                                                                      \
+        unsigned char* row_ = sm + kOffX + hf * 16384 + r * 128;                                               \
+        _Pragma("unroll") for (int jj = 0; jj < 8; ++jj)                                                      \
+            *reinterpret_cast<uint4*>(row_ + ((jj ^ (r & 7)) << 4)) =                                          \
+                make_uint4(pack_bf16x2(x[8 * jj], x[8 * jj + 1]), pack_bf16x2(x[8 * jj + 2], x[8 * jj + 3]),   \
+                           pack_bf16x2(x[8 * jj + 4], x[8 * jj + 5]), pack_bf16x2(x[8 * jj + 6], x[8 * jj + 7])); \
+    } while (0)
+
 // ------------------------------------------------------------------------------------------
 // 1. local transitions
 // ------------------------------------------------------------------------------------------
-__global__ void __maxnreg__(112)
+// 288 threads: registers are granted to warps in groups of four, so 12 warps' worth of the
+// 64 K-entry file caps this kernel at 168 registers per thread
+__global__ void __launch_bounds__(segk::kThreads, 1)
     gdn_prefill_seg_local_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace segk;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(sm);
-    uint64_t* wq_full = reinterpret_cast<uint64_t*>(sm + kOffBar);
-    uint64_t* wq_empty = wq_full + 1;
-    uint64_t* kfull = wq_full + 2;
-    uint64_t* kempty = wq_full + 4;
-    uint64_t* ufull = wq_full + 6;
-    uint64_t* uempty = wq_full + 7;
-    uint64_t* bar_p = wq_full + 8;
-    uint64_t* bar_u = wq_full + 10;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(wq_full + 12);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* empty = full + kStages;
+    uint64_t* bar_p = empty + kStages;
+    uint64_t* bar_u = bar_p + 1;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_u + 1);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_u + 1) + 1;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ss = blockIdx.x, hv = blockIdx.y;
+    const int ss = blockIdx.x, hv = blockIdx.y, half = blockIdx.z;  // half 0: beta (with u), 1: Phi
     const int hq = hv / (p.HV / p.H);
-    const int prod_warp = 2 * kGroupThreads / 32;
-    if (warp == prod_warp && lane == 0) {
+    if (warp == kMath / 32 && lane == 0) {
         tma_prefetch_desc(&maps.w);
         tma_prefetch_desc(&maps.qp);
         tma_prefetch_desc(&maps.k);
-        tma_prefetch_desc(&maps.qpp);
-        tma_prefetch_desc(&maps.oipp);
+        tma_prefetch_desc(half ? &maps.qpp : &maps.oipp);
     }
     pdl_wait();  // the workspace comes from the prep kernel
     pdl_trigger();
@@ -135,23 +140,21 @@ __global__ void __maxnreg__(112)
     if (sq.n < 0 || ss >= p.SS) return;  // a slot past the last segment (uniform across the CTA)
     int bos, eos;
     seq_bounds(p.cu, p.cu64, sq.n, p.T, bos, eos);
-    const int c0 = (ss - sq.sbase) * p.seg_m;
+    const int seg = ss - sq.sbase;
+    const int c0 = seg * p.seg_m;
     int nch = min(p.seg_m, sq.nc - c0);
     nch = max(0, min(nch, p.S - (sq.cbase + c0)));  // only a cu_seqlens that is not non-decreasing trims it
     if (nch <= 0) return;
     const int slot0 = sq.cbase + c0;
 
     if (tid == 0) {
-        mbar_init(wq_full, 1);
-        mbar_init(wq_empty, 2);  // one arrival per group once its MMA_P has completed
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(kfull + s, 1);
-            mbar_init(kempty + s, 2);  // one arrival per group once its MMA_U has completed
-            mbar_init(bar_p + s, 1);
-            mbar_init(bar_u + s, 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kMath / 32);
         }
-        mbar_init(ufull, 1);
-        mbar_init(uempty, 4);  // the four vn warps of group 0
+        mbar_init(bar_p, 1);
+        mbar_init(bar_u, 1);
+        *abort_flag = 0;
         mbar_fence_init();
     }
     if (warp == 0) tmem_alloc(tslot, kTmemCols);
@@ -160,137 +163,103 @@ __global__ void __maxnreg__(112)
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    if (warp == prod_warp) {
-        // Producer.  k stage c % 2 (k tile, gates) is refilled once both groups finished chunk c - 2;
-        // the single W / Q' buffer once both groups' MMA_P of chunk c - 1 completed; the single u
-        // buffer once group 0 formed chunk c - 1's vn.
+    if (warp == kMath / 32) {
+        // Producer: stage c % 2 gets chunk c's W, Q', K tiles, gates and (half 0) u once chunk
+        // c - 2 is done.
         if (lane == 0) {
             for (int c = 0; c < nch; ++c) {
-                const int slot = slot0 + c, wr = slot * kChunk, t0 = bos + (c0 + c) * kChunk;
-                if (c >= 2 && !mbar_wait(kempty + (c & 1), (uint32_t)(((c >> 1) - 1) & 1), p.status, kErrScanTmaTimeout))
+                if (c >= kStages && !mbar_wait(empty + (c % kStages), (uint32_t)((c / kStages - 1) & 1), p.status,
+                                               kErrScanTmaTimeout))
                     break;
-                unsigned char* ks = sm + kOffK + (c & 1) * kKStage;
-                mbar_arrive_expect_tx(kfull + (c & 1), 16384 + 1024);
-                tma_load_3d(ks, &maps.k, 0, hq, t0, kfull + (c & 1));
-                tma_load_3d(ks + 8192, &maps.k, 64, hq, t0, kfull + (c & 1));
-                bulk_load(ks + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, kfull + (c & 1));
-                if (c >= 1 && !mbar_wait(wq_empty, (uint32_t)((c - 1) & 1), p.status, kErrScanTmaTimeout)) break;
-                mbar_arrive_expect_tx(wq_full, 32768);
-                tma_load_3d(sm + kOffWQ, &maps.w, 0, wr, hv, wq_full);
-                tma_load_3d(sm + kOffWQ + 8192, &maps.qp, 0, wr, hv, wq_full);
-                tma_load_3d(sm + kOffWQ + 16384, &maps.w, 64, wr, hv, wq_full);
-                tma_load_3d(sm + kOffWQ + 24576, &maps.qp, 64, wr, hv, wq_full);
-                if (c >= 1 && !mbar_wait(uempty, (uint32_t)((c - 1) & 1), p.status, kErrScanTmaTimeout)) break;
-                mbar_arrive_expect_tx(ufull, 32768);
-                bulk_load(sm + kOffU, p.u + cg_off(hv, p.S, slot, 0), 32768, ufull);
+                unsigned char* st = sm + (c % kStages) * kStage;
+                uint64_t* bar = full + (c % kStages);
+                const int slot = slot0 + c, wr = slot * kChunk, t0 = bos + (c0 + c) * kChunk;
+                mbar_arrive_expect_tx(bar, kTxTiles + (half == 0 ? 32768u : 0u));
+                tma_load_3d(st + kOffWQ, &maps.w, 0, wr, hv, bar);
+                tma_load_3d(st + kOffWQ + 8192, &maps.qp, 0, wr, hv, bar);
+                tma_load_3d(st + kOffWQ + 16384, &maps.w, 64, wr, hv, bar);
+                tma_load_3d(st + kOffWQ + 24576, &maps.qp, 64, wr, hv, bar);
+                tma_load_3d(st + kOffK, &maps.k, 0, hq, t0, bar);
+                tma_load_3d(st + kOffK + 8192, &maps.k, 64, hq, t0, bar);
+                bulk_load(st + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, bar);
+                if (half == 0) bulk_load(st + kOffU, p.u + cg_off(hv, p.S, slot, 0), 32768, bar);
             }
         }
     } else {
-        // ---- math: group g, thread (r, hf) = TMEM lane r, state columns 64 hf .. 64 hf + 63 ----
-        const int g = warp >> 3, gw = warp & 7;
-        const int r = lane + 32 * (gw & 3), hf = gw >> 2;
-        const int gt = tid - g * kGroupThreads;  // thread index inside the group
-        const uint32_t lanebits = (uint32_t)(32 * (gw & 3)) << 16;
-        const uint32_t tP = tmem + lanebits + 256u * g + 64u * hf;  // this thread's 64 P columns
-        const uint32_t tX = tP + 128u;                                // and 64 X columns
-        unsigned char* xb = sm + kOffX + g * 32768;
-        const uint32_t sxb = sbase + kOffX + (uint32_t)g * 32768u;
-        unsigned char* ob = sm + kOffO + g * 16384;
-        const CUtensorMap* omap = g ? &maps.qpp : &maps.oipp;
-        // X starts as 0 (beta) or I (Phi): in TMEM (fp32) and as the bf16 MMA operand
-        {
-            uint32_t z[32];
+        // ---- math warps: thread (r, hf) = TMEM lane r, state columns 64 hf .. 64 hf + 63 ----
+        const int r = lane + 32 * (warp & 3), hf = warp >> 2;
+        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * hf;
+        float x[64];  // X row r (K index), columns 64 hf + j
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) z[j] = __float_as_uint((g == 1 && r == 64 * hf + 32 * blk + j) ? 1.f : 0.f);
-                tmem_st32(tX + 32u * blk, z);
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    *reinterpret_cast<uint4*>(xb + hf * 16384 + r * 128 + (((4 * blk + q4) ^ (r & 7)) << 4)) =
-                        make_uint4(pack_bf16x2(__uint_as_float(z[8 * q4]), __uint_as_float(z[8 * q4 + 1])),
-                                   pack_bf16x2(__uint_as_float(z[8 * q4 + 2]), __uint_as_float(z[8 * q4 + 3])),
-                                   pack_bf16x2(__uint_as_float(z[8 * q4 + 4]), __uint_as_float(z[8 * q4 + 5])),
-                                   pack_bf16x2(__uint_as_float(z[8 * q4 + 6]), __uint_as_float(z[8 * q4 + 7])));
-            }
-            tmem_st_wait();
-        }
+        for (int j = 0; j < 64; ++j) x[j] = (half == 1 && r == 64 * hf + j) ? 1.f : 0.f;
+        // bf16 copy of X: MN-major SW128 B operand of MMA_P, column block hf, row r
+        GDN_SEG_WRITE_XB();
         constexpr uint32_t idesc_p = umma_idesc_bf16(128, 128, false, true);
         constexpr uint32_t idesc_u = umma_idesc_bf16(128, 128, true, true);
-        const bool dbg = g == 0;
+        const CUtensorMap* omap = half ? &maps.qpp : &maps.oipp;
+        float gamma = 1.f;
+        const bool dbg = true;
         long long tp = clock64();
         (void)dbg;
-        float gamma = 1.f;
-        bool okc = true;  // every bounded wait of this thread so far succeeded
         int c = 0;
         for (; c < nch; ++c) {
             const uint32_t ph = (uint32_t)(c & 1);
-            bool ok = mbar_wait(kfull + (c & 1), (uint32_t)((c >> 1) & 1), p.status, kErrScanTmaTimeout) && okc;
-            ok = mbar_wait(wq_full, ph, p.status, kErrScanTmaTimeout) && ok;
+            if (!mbar_wait(full + (c % kStages), (uint32_t)((c / kStages) & 1), p.status, kErrScanTmaTimeout))
+                *abort_flag = 1;
             GDN_PH_ACC(dbg, 0, tp);
-            if (gt == 128) tma_store_wait_read();  // the previous output tile has left the staging buffer
-            fence_async_smem();                     // X copy (generic stores) -> the tensor core
+            fence_async_smem();  // this thread's X copy (generic stores) -> the tensor core
             tc_fence_before();
-            // a wait that gave up anywhere in the group stops the whole group (uniform break)
-            if (!named_bar_and(1 + g, kGroupThreads, ok)) break;
-            tc_fence_after();
+            named_bar_sync(1, kMath);
             GDN_PH_ACC(dbg, 1, tp);
-            const unsigned char* ks = sm + kOffK + (c & 1) * kKStage;
-            const uint32_t sks = sbase + kOffK + (uint32_t)(c & 1) * kKStage;
-            const float* G4 = reinterpret_cast<const float*>(ks + kOffG);
+            if (*abort_flag) break;  // written only before this barrier
+            tc_fence_after();
+            const unsigned char* st = sm + (c % kStages) * kStage;
+            const uint32_t sst = sbase + (uint32_t)(c % kStages) * kStage;
+            const float* G4 = reinterpret_cast<const float*>(st + kOffG);
             const int slot = slot0 + c;
             const int t0 = bos + (c0 + c) * kChunk;
             const int L = min(kChunk, eos - t0);
             const float GL = G4[(L - 1) * 4];
-            const float eL = __expf(GL);
-            // MMA_P: [W; Q'] (128 x 128, K-major) x X (128 x 128, MN-major) -> P
-            if (gt == 0) {
+            // MMA_P: [W; Q'] (128 x 128, K-major) x X (128 x 128, MN-major) -> TMEM columns 0-127.
+            // The beta half starts from X = 0: its first product is zero and is not formed.
+            const bool zeroP = half == 0 && c == 0;
+            const uint32_t php = (uint32_t)((c - (half == 0 ? 1 : 0)) & 1);  // bar_p phase (one commit per product)
+            if (tid == 0 && !zeroP) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    umma_bf16(tmem + 256u * g,
-                              umma_desc_sw128(sbase + kOffWQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
-                              umma_desc_sw128(sxb + 2048u * kk, 16384, 1024), idesc_p, kk > 0);
-                umma_commit(bar_p + g);
+                    umma_bf16(tmem,
+                              umma_desc_sw128(sst + kOffWQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+                              umma_desc_sw128(sbase + kOffX + 2048u * kk, 16384, 1024), idesc_p, kk > 0);
+                umma_commit(bar_p);
             }
-            ok = mbar_wait(bar_p + g, ph, p.status, kErrScanMmaTimeout);
+            bool ok = zeroP || mbar_wait(bar_p, php, p.status, kErrScanMmaTimeout);
             tc_fence_after();
-            if (gt == 0) mbar_arrive(wq_empty);  // this group's MMA_P has read W / Q'
             GDN_PH_ACC(dbg, 2, tp);
-            // X <- e^{G_L} X in TMEM: MMA_U then accumulates K^T vn onto it
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-                uint32_t d[32];
-                tmem_ld32_async(tX + 32u * blk, d);
-                tmem_ld_wait();
-                tmem_regs_ready(d);
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    const float2 v2 = mul2(make_float2(eL, eL), make_float2(__uint_as_float(d[j]), __uint_as_float(d[j + 1])));
-                    d[j] = __float_as_uint(v2.x);
-                    d[j + 1] = __float_as_uint(v2.y);
-                }
-                tmem_st32(tX + 32u * blk, d);
-            }
             if (r < 64) {
                 // vn = ([u | 0] - W X) e^{G_L - G_r} / |k_r|  -> bf16 hi + lo, token row r
-                if (g == 0 && !mbar_wait(ufull, ph, p.status, kErrScanTmaTimeout)) ok = false;
+                bool okv = true;
                 const float4 g4r = *reinterpret_cast<const float4*>(G4 + r * 4);  // {G, e^G, beta, rk}
                 const float ed = __expf(GL - g4r.x) * g4r.w;
-                const float* Us = reinterpret_cast<const float*>(sm + kOffU);
-                unsigned char* rh = xb + hf * 8192 + r * 128;
+                const float* Us = reinterpret_cast<const float*>(st + kOffU);
+                unsigned char* rh = sm + kOffX + hf * 8192 + r * 128;
                 unsigned char* rl = rh + 16384;
                 const int hA = (r >> 2) & 1;
 #pragma unroll
                 for (int blk = 0; blk < 2; ++blk) {
                     uint32_t d[32];
-                    tmem_ld32_async(tP + 32u * blk, d);
-                    tmem_ld_wait();
-                    tmem_regs_ready(d);
+                    if (zeroP) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) d[j] = 0u;
+                    } else {
+                        tmem_ld32_async(tl + 32u * blk, d);
+                        tmem_ld_wait();
+                        tmem_regs_ready(d);
+                    }
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int jj = 4 * blk + q4;  // 8-column group inside this thread's 64 columns
                         float uu[8];
-                        if (g == 0) {
+                        if (half == 0) {
                             const int cg = 8 * hf + jj;
                             const float4 x0 = *reinterpret_cast<const float4*>(Us + (cg * 64 + r) * 8 + 4 * hA);
                             const float4 x1 = *reinterpret_cast<const float4*>(Us + (cg * 64 + r) * 8 + 4 * (hA ^ 1));
@@ -318,123 +287,122 @@ __global__ void __maxnreg__(112)
                         *reinterpret_cast<uint4*>(rl + ((jj ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
                 }
-                if (g == 0) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(uempty);  // this warp's u rows are consumed
+                // warps 0, 1, 4, 5 alone gate MMA_U
+                GDN_PH_ACC(dbg, 3, tp);
+                fence_async_smem();
+                tc_fence_before();
+                okv = named_bar_and(2, 128, ok && okv);
+                tc_fence_after();
+                GDN_PH_ACC(dbg, 4, tp);
+                // MMA_U: K^T (128 x 64 tokens, MN-major) x (vn_hi + vn_lo) -> TMEM columns 128-255
+                if (okv && tid == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16(tmem + 128, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
+                                  umma_desc_sw128(sbase + kOffX + 2048u * kk, 8192, 1024), idesc_u, kk > 0);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16(tmem + 128, umma_desc_sw128(sst + kOffK + 2048u * kk, 8192, 1024),
+                                  umma_desc_sw128(sbase + kOffX + 16384u + 2048u * kk, 8192, 1024), idesc_u, true);
+                    umma_commit(bar_u);
                 }
+                ok = okv;
             } else {
-                // output operand row m = r - 64: oi'' = Q' beta (group 0) or Q'' = Q' Phi (group 1), bf16,
-                // staged SW128 for one TMA store per 64 columns
+                // output operand row m = r - 64: oi'' = Q' beta (half 0) or Q'' = Q' Phi (half 1),
+                // staged SW128 in the stage's (consumed) W / Q' area, then one TMA store per 64 columns
                 const int m = r - 64;
-                unsigned char* orow = ob + hf * 8192 + m * 128;
+                unsigned char* orow = sm + (c % kStages) * kStage + kOffWQ + hf * 8192 + m * 128;
 #pragma unroll
                 for (int blk = 0; blk < 2; ++blk) {
                     uint32_t d[32];
-                    tmem_ld32_async(tP + 32u * blk, d);
-                    tmem_ld_wait();
-                    tmem_regs_ready(d);
+                    if (zeroP) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) d[j] = 0u;
+                    } else {
+                        tmem_ld32_async(tl + 32u * blk, d);
+                        tmem_ld_wait();
+                        tmem_regs_ready(d);
+                    }
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int jj = 4 * blk + q4;
-                        *reinterpret_cast<uint4*>(orow + ((jj ^ (m & 7)) << 4)) =
-                            make_uint4(pack_bf16x2(__uint_as_float(d[8 * q4]), __uint_as_float(d[8 * q4 + 1])),
-                                       pack_bf16x2(__uint_as_float(d[8 * q4 + 2]), __uint_as_float(d[8 * q4 + 3])),
-                                       pack_bf16x2(__uint_as_float(d[8 * q4 + 4]), __uint_as_float(d[8 * q4 + 5])),
-                                       pack_bf16x2(__uint_as_float(d[8 * q4 + 6]), __uint_as_float(d[8 * q4 + 7])));
+                        uint32_t pk[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            pk[e] = pack_bf16x2(__uint_as_float(d[8 * q4 + 2 * e]), __uint_as_float(d[8 * q4 + 2 * e + 1]));
+                        *reinterpret_cast<uint4*>(orow + ((jj ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     }
                 }
+                fence_async_smem();
+                named_bar_sync(3, 128);  // the four output warps
+                if (tid == 64) {         // warp 2, lane 0: store the 64 x 128 tile (two SW128 boxes)
+                    unsigned char* ob = sm + (c % kStages) * kStage + kOffWQ;
+                    tma_store_3d(omap, 0, slot * kChunk, hv, ob);
+                    tma_store_3d(omap, 64, slot * kChunk, hv, ob + 8192);
+                    tma_store_commit();
+                }
             }
-            GDN_PH_ACC(dbg, 3, tp);
-            tmem_st_wait();      // the scaled X is in TMEM
-            fence_async_smem();  // vn and the output tile (generic stores) -> the tensor core / TMA
-            tc_fence_before();
-            ok = named_bar_and(1 + g, kGroupThreads, ok);
-            tc_fence_after();
-            GDN_PH_ACC(dbg, 4, tp);
-            // MMA_U: K^T (128 x 64 tokens, MN-major) x (vn_hi + vn_lo), accumulated onto X
-            if (ok && gt == 0) {
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16(tmem + 256u * g + 128u, umma_desc_sw128(sks + 2048u * kk, 8192, 1024),
-                              umma_desc_sw128(sxb + 2048u * kk, 8192, 1024), idesc_u, true);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16(tmem + 256u * g + 128u, umma_desc_sw128(sks + 2048u * kk, 8192, 1024),
-                              umma_desc_sw128(sxb + 16384u + 2048u * kk, 8192, 1024), idesc_u, true);
-                umma_commit(bar_u + g);
-            }
-            if (gt == 128) {  // the output tile: two SW128 boxes of 64 columns
-                tma_store_3d(omap, 0, slot * kChunk, hv, ob);
-                tma_store_3d(omap, 64, slot * kChunk, hv, ob + 8192);
-                tma_store_commit();
-            }
-            GDN_PH_ACC(dbg, 5, tp);
             // an MMA_U that was not issued (a wait gave up) also fails this bounded wait
-            if (ok) ok = mbar_wait(bar_u + g, ph, p.status, kErrScanMmaTimeout);
+            GDN_PH_ACC(dbg, 5, tp);
+            if (ok) ok = mbar_wait(bar_u, ph, p.status, kErrScanMmaTimeout);
             tc_fence_after();
-            if (gt == 0) mbar_arrive(kempty + (c & 1));  // this group is done with the k tile and gates
             GDN_PH_ACC(dbg, 6, tp);
-            // bf16 copy of the new X for the next MMA_P
+            {
+                const float eL = __expf(GL);
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-                uint32_t d[32];
-                tmem_ld32_async(tX + 32u * blk, d);
-                tmem_ld_wait();
-                tmem_regs_ready(d);
+                for (int blk = 0; blk < 2; ++blk) {
+                    uint32_t d[32];
+                    tmem_ld32_async(tl + 128u + 32u * blk, d);
+                    tmem_ld_wait();
+                    tmem_regs_ready(d);
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    *reinterpret_cast<uint4*>(xb + hf * 16384 + r * 128 + (((4 * blk + q4) ^ (r & 7)) << 4)) =
-                        make_uint4(pack_bf16x2(__uint_as_float(d[8 * q4]), __uint_as_float(d[8 * q4 + 1])),
-                                   pack_bf16x2(__uint_as_float(d[8 * q4 + 2]), __uint_as_float(d[8 * q4 + 3])),
-                                   pack_bf16x2(__uint_as_float(d[8 * q4 + 4]), __uint_as_float(d[8 * q4 + 5])),
-                                   pack_bf16x2(__uint_as_float(d[8 * q4 + 6]), __uint_as_float(d[8 * q4 + 7])));
+                    for (int j = 0; j < 32; j += 2) {
+                        const float2 xn = fma2(make_float2(eL, eL), make_float2(x[32 * blk + j], x[32 * blk + j + 1]),
+                                               make_float2(__uint_as_float(d[j]), __uint_as_float(d[j + 1])));
+                        x[32 * blk + j] = xn.x;
+                        x[32 * blk + j + 1] = xn.y;
+                    }
+                }
+                gamma *= eL;
             }
-            gamma *= eL;
-            okc = ok;
+            // the stage's operands are consumed (and its output tile read by the TMA store)
+            if (tid == 64) tma_store_wait_read();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + (c % kStages));
+            if (!ok) *abort_flag = 1;
+            GDN_SEG_WRITE_XB();
             GDN_PH_ACC(dbg, 7, tp);
         }
         if (c < nch) {
             // gave up: let copies already in flight land (bounded) before the CTA exits
-            if (gt == 0) {
-                for (int cc = c; cc < min(nch, c + 2); ++cc)
-                    mbar_wait(kfull + (cc & 1), (uint32_t)((cc >> 1) & 1), nullptr, 0);
-                mbar_wait(wq_full, (uint32_t)(c & 1), nullptr, 0);
-                if (g == 0) mbar_wait(ufull, (uint32_t)(c & 1), nullptr, 0);
-            }
+            if (tid == 0)
+                for (int cc = c + 1; cc < min(nch, c + kStages); ++cc)
+                    mbar_wait(full + (cc % kStages), (uint32_t)((cc / kStages) & 1), nullptr, 0);
         } else {
-            // segment transition: B = beta_end (group 0), D = Phi_end - gamma I and gamma (group 1)
             const size_t seg_i = (size_t)hv * p.SS + ss;
+            if (half == 0) {
+                // B = beta_end, column-group major [16][128][8] f32
+                float* Bp = p.seg_B + seg_i * 128 * 128;
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-                uint32_t d[32];
-                tmem_ld32_async(tX + 32u * blk, d);
-                tmem_ld_wait();
-                tmem_regs_ready(d);
-                if (g == 0) {
-                    float* Bp = p.seg_B + seg_i * 128 * 128;  // column-group major [16][128][8] f32
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        float4* dst = reinterpret_cast<float4*>(Bp + ((8 * hf + 4 * blk + q4) * 128 + r) * 8);
-                        dst[0] = make_float4(__uint_as_float(d[8 * q4]), __uint_as_float(d[8 * q4 + 1]),
-                                             __uint_as_float(d[8 * q4 + 2]), __uint_as_float(d[8 * q4 + 3]));
-                        dst[1] = make_float4(__uint_as_float(d[8 * q4 + 4]), __uint_as_float(d[8 * q4 + 5]),
-                                             __uint_as_float(d[8 * q4 + 6]), __uint_as_float(d[8 * q4 + 7]));
-                    }
-                } else {
-                    float x[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        x[j] = __uint_as_float(d[j]) - ((r == 64 * hf + 32 * blk + j) ? gamma : 0.f);
-                    uint4* dst = reinterpret_cast<uint4*>(p.seg_D + (seg_i * 128 + r) * 128 + 64 * hf + 32 * blk);
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4)
-                        dst[q4] = make_uint4(pack_bf16x2(x[8 * q4], x[8 * q4 + 1]), pack_bf16x2(x[8 * q4 + 2], x[8 * q4 + 3]),
-                                             pack_bf16x2(x[8 * q4 + 4], x[8 * q4 + 5]), pack_bf16x2(x[8 * q4 + 6], x[8 * q4 + 7]));
+                for (int jj = 0; jj < 8; ++jj) {
+                    float4* dst = reinterpret_cast<float4*>(Bp + ((8 * hf + jj) * 128 + r) * 8);
+                    dst[0] = make_float4(x[8 * jj], x[8 * jj + 1], x[8 * jj + 2], x[8 * jj + 3]);
+                    dst[1] = make_float4(x[8 * jj + 4], x[8 * jj + 5], x[8 * jj + 6], x[8 * jj + 7]);
                 }
+            } else {
+                // D = Phi_end - gamma I, row-major [128][128] bf16 (row = output k index)
+#pragma unroll
+                for (int j = 0; j < 64; ++j)
+                    if (r == 64 * hf + j) x[j] -= gamma;
+                uint4* dst = reinterpret_cast<uint4*>(p.seg_D + (seg_i * 128 + r) * 128 + 64 * hf);
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj)
+                    dst[jj] = make_uint4(pack_bf16x2(x[8 * jj], x[8 * jj + 1]), pack_bf16x2(x[8 * jj + 2], x[8 * jj + 3]),
+                                         pack_bf16x2(x[8 * jj + 4], x[8 * jj + 5]), pack_bf16x2(x[8 * jj + 6], x[8 * jj + 7]));
+                if (tid == 0) p.seg_gamma[seg_i] = gamma;
             }
-            if (g == 1 && gt == 0) p.seg_gamma[seg_i] = gamma;
         }
-        if (gt == 128) tma_store_wait_all();  // the operand stores are complete before the grid ends
+        if (tid == 64) tma_store_wait_all();  // the operand stores are complete before the grid ends
     }
     tc_fence_before();
     __syncthreads();
@@ -583,23 +551,31 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
 // ------------------------------------------------------------------------------------------
 namespace sego {
 constexpr int kThreads = 256;
-constexpr uint32_t kOffQ = 0;        // Q'' 2 atoms [64][128 B]
-constexpr uint32_t kOffO = 16384;    // oi'' 2 atoms [64][128 B]
-constexpr uint32_t kOffH = 32768;    // h_s 2 atoms [128 K][128 B] (64 V columns each)
-constexpr uint32_t kTx = 16384 + 16384 + 32768;
-constexpr uint32_t kOffBar = 65536;
-constexpr uint32_t kSmem = kOffBar + 16 + 1024;
+constexpr int kGroup = 4;            // chunks per CTA (all in one segment: they share h_s)
+constexpr uint32_t kOffH = 0;        // h_s 2 atoms [128 K][128 B] (64 V columns each), SW128
+constexpr uint32_t kOffBuf = 32768;  // 2 buffers of {Q'' 2 atoms [64][128 B], oi'' 2 atoms}; after the
+                                     // products the buffer holds the fp32 [64][128] pre-output tile
+constexpr uint32_t kBuf = 32768;
+constexpr uint32_t kOffBar = kOffBuf + 2 * kBuf;  // h, buf[2]
+constexpr uint32_t kSmem = kOffBar + 32 + 1024;
 }  // namespace sego
+
+// fp32 [64][128] tile: float4 unit u of row r sits at unit u ^ (r & 7) (conflict-free row-fragment
+// writes and 32-byte row reads)
+__device__ __forceinline__ uint32_t pre_off(int r, int c) {
+    return (uint32_t)r * 512u + ((((uint32_t)c >> 2) ^ ((uint32_t)r & 7u)) << 4) + ((uint32_t)c & 3u) * 4u;
+}
 
 __global__ void __launch_bounds__(sego::kThreads)
     gdn_prefill_seg_out_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace sego;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* bar_h = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* bar_b = bar_h + 1;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;
-    const int slot = blockIdx.x, hv = blockIdx.y;
+    const int ss = blockIdx.x, hv = blockIdx.y;
     if (tid == 0) {
         tma_prefetch_desc(&maps.qpp);
         tma_prefetch_desc(&maps.oipp);
@@ -607,73 +583,117 @@ __global__ void __launch_bounds__(sego::kThreads)
     }
     pdl_wait();
     pdl_trigger();
-    if (slot == 0 && hv == 0) zero_unowned_tokens(p, tid, kThreads);
-    const SegSeq sq = warp_seg_seq(p, kByChunk, slot);
-    if (sq.n < 0) return;
+    if (ss == 0 && hv == 0 && blockIdx.z == 0) zero_unowned_tokens(p, tid, kThreads);
+    const SegSeq sq = warp_seg_seq(p, kBySeg, ss);
+    if (sq.n < 0 || ss >= p.SS) return;
     int bos, eos;
     seq_bounds(p.cu, p.cu64, sq.n, p.T, bos, eos);
-    const int c = slot - sq.cbase;
-    const int ss = sq.sbase + c / p.seg_m;
-    if (ss >= p.SS) return;  // only a cu_seqlens that is not non-decreasing gets here
-    const int t0 = bos + c * kChunk;
-    const int L = min(kChunk, eos - t0);
+    const int seg_c0 = (ss - sq.sbase) * p.seg_m;  // first chunk of the segment (within the sequence)
+    const int c0 = seg_c0 + (int)blockIdx.z * kGroup;
+    int nch = min(kGroup, min(seg_c0 + p.seg_m, sq.nc) - c0);
+    nch = min(nch, p.S - (sq.cbase + c0));  // only a cu_seqlens that is not non-decreasing trims it
+    if (nch <= 0) return;
     if (tid == 0) {
-        mbar_init(bar, 1);
+        mbar_init(bar_h, 1);
+        mbar_init(bar_b, 1);
+        mbar_init(bar_b + 1, 1);
         mbar_fence_init();
     }
     __syncthreads();
+    auto issue = [&](int c) {  // thread 0: chunk c's Q'' and oi'' into buffer c % 2
+        unsigned char* bf = sm + kOffBuf + (c & 1) * kBuf;
+        const int row = (sq.cbase + c0 + c) * kChunk;
+        mbar_arrive_expect_tx(bar_b + (c & 1), 32768);
+        tma_load_3d(bf, &maps.qpp, 0, row, hv, bar_b + (c & 1));
+        tma_load_3d(bf + 8192, &maps.qpp, 64, row, hv, bar_b + (c & 1));
+        tma_load_3d(bf + 16384, &maps.oipp, 0, row, hv, bar_b + (c & 1));
+        tma_load_3d(bf + 24576, &maps.oipp, 64, row, hv, bar_b + (c & 1));
+    };
     if (tid == 0) {
-        mbar_arrive_expect_tx(bar, kTx);
-        tma_load_3d(sm + kOffQ, &maps.qpp, 0, slot * kChunk, hv, bar);
-        tma_load_3d(sm + kOffQ + 8192, &maps.qpp, 64, slot * kChunk, hv, bar);
-        tma_load_3d(sm + kOffO, &maps.oipp, 0, slot * kChunk, hv, bar);
-        tma_load_3d(sm + kOffO + 8192, &maps.oipp, 64, slot * kChunk, hv, bar);
-        tma_load_3d(sm + kOffH, &maps.seghb, 0, ss * 128, hv, bar);
-        tma_load_3d(sm + kOffH + 16384, &maps.seghb, 64, ss * 128, hv, bar);
+        mbar_arrive_expect_tx(bar_h, 32768);
+        tma_load_3d(sm + kOffH, &maps.seghb, 0, ss * 128, hv, bar_h);
+        tma_load_3d(sm + kOffH + 16384, &maps.seghb, 64, ss * 128, hv, bar_h);
+        issue(0);
+        if (nch > 1) issue(1);
     }
-    if (!mbar_wait(bar, 0, p.status, kErrScanTmaTimeout)) {
-        if (tid == 0) mbar_wait(bar, 0, nullptr, 0);
-        return;
-    }
-    // oi = Aqk u of the chunk (prep kernel, column-group major [16][64][8] bf16)
-    const uint16_t* oi_slot = p.oi + cg_off(hv, p.S, slot, 0);
+    bool ok = mbar_wait(bar_h, 0, p.status, kErrScanTmaTimeout);
     // warp w: output rows 16 (w & 3) .. +15, columns 64 (w >> 2) .. +63
     const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
-    float acc[8][4];
+    int c = 0;
+    for (; c < nch; ++c) {
+        ok = mbar_wait(bar_b + (c & 1), (uint32_t)((c >> 1) & 1), p.status, kErrScanTmaTimeout) && ok;
+        if (!__syncthreads_and(ok)) break;
+        unsigned char* bf = sm + kOffBuf + (c & 1) * kBuf;
+        float acc[8][4];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+        for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+            for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 #pragma unroll
-    for (int k0 = 0; k0 < 128; k0 += 16) {
-        uint32_t a[4];
-        ldsm_x4(a[0], a[1], a[2], a[3], sm + kOffQ + sw128_off(r0 + (lane & 15), k0 + ((lane >> 4) << 3), 8192));
+        for (int k0 = 0; k0 < 128; k0 += 16) {
+            uint32_t a[4];
+            ldsm_x4(a[0], a[1], a[2], a[3], bf + sw128_off(r0 + (lane & 15), k0 + ((lane >> 4) << 3), 8192));
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-            uint32_t b0, b1, b2, b3;
-            const int kr = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
-            const int cc = n0 + 16 * np + ((lane >> 4) << 3);
-            ldsm_x4_t(b0, b1, b2, b3, sm + kOffH + sw128_off(kr, cc, 16384));
-            mma_bf16(acc[2 * np], a, b0, b1);
-            mma_bf16(acc[2 * np + 1], a, b2, b3);
+            for (int np = 0; np < 4; ++np) {
+                uint32_t b0, b1, b2, b3;
+                const int kr = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
+                const int cc = n0 + 16 * np + ((lane >> 4) << 3);
+                ldsm_x4_t(b0, b1, b2, b3, sm + kOffH + sw128_off(kr, cc, 16384));
+                mma_bf16(acc[2 * np], a, b0, b1);
+                mma_bf16(acc[2 * np + 1], a, b2, b3);
+            }
         }
-    }
+        // + oi'' (bf16 tile in this buffer)
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-        const int row = r0 + gq + 8 * hh;
-        if (row >= L) continue;
-        uint16_t* dst = p.out + ((size_t)(t0 + row) * p.HV + hv) * kD;
+        for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const int col = n0 + 8 * nt + 2 * tq;
-            const uint32_t oo = *reinterpret_cast<const uint32_t*>(sm + kOffO + sw128_off(row, col, 8192));
-            const uint32_t oc = *reinterpret_cast<const uint32_t*>(oi_slot + (col >> 3) * 512 + row * 8 + (col & 7));
-            const float2 o2 = add2(add2(make_float2(acc[nt][2 * hh], acc[nt][2 * hh + 1]),
-                                        make_float2(__uint_as_float(oo << 16), __uint_as_float(oo & 0xffff0000u))),
-                                   make_float2(__uint_as_float(oc << 16), __uint_as_float(oc & 0xffff0000u)));
-            *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16x2(p.scale * o2.x, p.scale * o2.y);
+            for (int hh = 0; hh < 2; ++hh) {
+                const int row = r0 + gq + 8 * hh, col = n0 + 8 * nt + 2 * tq;
+                const uint32_t oo = *reinterpret_cast<const uint32_t*>(bf + 16384 + sw128_off(row, col, 8192));
+                acc[nt][2 * hh] += __uint_as_float(oo << 16);
+                acc[nt][2 * hh + 1] += __uint_as_float(oo & 0xffff0000u);
+            }
+        __syncthreads();  // every warp has read Q'' and oi'': the buffer takes the fp32 tile
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                const int row = r0 + gq + 8 * hh, col = n0 + 8 * nt + 2 * tq;
+                *reinterpret_cast<float2*>(bf + pre_off(row, col)) = make_float2(acc[nt][2 * hh], acc[nt][2 * hh + 1]);
+            }
+        __syncthreads();
+        // o = scale (tile + oi), oi = Aqk u of the chunk (prep, column-group major [16][64][8] bf16);
+        // thread = (row, 8-column group): 16-byte loads and stores
+        {
+            const int slot = sq.cbase + c0 + c;
+            const int t0 = bos + (c0 + c) * kChunk;
+            const int L = min(kChunk, eos - t0);
+            const uint16_t* oi_slot = p.oi + cg_off(hv, p.S, slot, 0);
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+                const int idx = tid + 256 * it, row = idx >> 4, cg = idx & 15;
+                if (row < L) {
+                    const float4 x0 = *reinterpret_cast<const float4*>(bf + pre_off(row, 8 * cg));
+                    const float4 x1 = *reinterpret_cast<const float4*>(bf + pre_off(row, 8 * cg + 4));
+                    const uint4 oc = *reinterpret_cast<const uint4*>(oi_slot + cg * 512 + row * 8);
+                    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    const uint32_t ow[4] = {oc.x, oc.y, oc.z, oc.w};
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        pk[e] = pack_bf16x2(p.scale * (xs[2 * e] + __uint_as_float(ow[e] << 16)),
+                                            p.scale * (xs[2 * e + 1] + __uint_as_float(ow[e] & 0xffff0000u)));
+                    *reinterpret_cast<uint4*>(p.out + ((size_t)(t0 + row) * p.HV + hv) * kD + 8 * cg) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+            }
         }
+        fence_async_smem();  // this thread's accesses to the buffer come before the next TMA write
+        __syncthreads();     // the buffer is free: chunk c + 2 may load into it
+        if (tid == 0 && c + 2 < nch) issue(c + 2);
     }
+    if (c < nch && tid == 0)  // gave up: let copies in flight land (bounded) before the CTA exits
+        for (int cc = c; cc < min(nch, c + 2); ++cc) mbar_wait(bar_b + (cc & 1), (uint32_t)((cc >> 1) & 1), nullptr, 0);
 }
 
 int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream) {
@@ -686,14 +706,14 @@ int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream
         return -1;
     // segment slots actually used: sum_n ceil(nc_n / m) <= min(SS, ceil(T / 64 / m) + N - 1)
     const long long segs = std::min<long long>(p.SS, ((long long)p.T + 64LL * p.seg_m - 1) / (64LL * p.seg_m) + p.N - 1);
-    if (launch_pdl(gdn_prefill_seg_local_kernel, dim3((unsigned)std::max<long long>(segs, 1), p.HV),
+    if (launch_pdl(gdn_prefill_seg_local_kernel, dim3((unsigned)std::max<long long>(segs, 1), p.HV, 2),
                    dim3(segk::kThreads), segk::kSmem, stream, p, maps) != cudaSuccess)
         return -1;
     if (launch_pdl(gdn_prefill_seg_chain_kernel, dim3(kD / segc::BV, p.N, p.HV), dim3(segc::kThreads), segc::kSmem,
                    stream, p, maps) != cudaSuccess)
         return -1;
-    const long long chunks = std::min<long long>(p.S, ((long long)p.T + 63) / 64 + p.N - 1);
-    if (launch_pdl(gdn_prefill_seg_out_kernel, dim3((unsigned)std::max<long long>(chunks, 1), p.HV),
+    if (launch_pdl(gdn_prefill_seg_out_kernel,
+                   dim3((unsigned)std::max<long long>(segs, 1), p.HV, (p.seg_m + sego::kGroup - 1) / sego::kGroup),
                    dim3(sego::kThreads), sego::kSmem, stream, p, maps) != cudaSuccess)
         return -1;
     return 0;
