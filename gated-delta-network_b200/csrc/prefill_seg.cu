@@ -19,7 +19,7 @@
 //   2. gdn_prefill_seg_chain_kernel, one CTA per (8 state columns, sequence, v-head): the short
 //      serial chain over segments, h_{s+1} = gamma h_s + D h_s + B; it records each h_s (bf16,
 //      the output operand) and writes the final state.
-//   3. gdn_prefill_seg_out_kernel, one CTA per (4 chunks of a segment, v-head):
+//   3. gdn_prefill_seg_out_kernel, one CTA per (2 chunks of a segment, v-head), one tcgen05 MMA:
 //      o_j = scale (Q''_j h_s + oi''_j + oi_j), oi_j = Aqk u from the prep.
 //
 // Per chunk the local kernel does what the single-pass scan does (two dependent products), on a
@@ -551,30 +551,24 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
 // ------------------------------------------------------------------------------------------
 namespace sego {
 constexpr int kThreads = 256;
-constexpr int kGroup = 4;            // chunks per CTA (all in one segment: they share h_s)
-constexpr uint32_t kOffH = 0;        // h_s 2 atoms [128 K][128 B] (64 V columns each), SW128
-constexpr uint32_t kOffBuf = 32768;  // 2 buffers of {Q'' 2 atoms [64][128 B], oi'' 2 atoms}; after the
-                                     // products the buffer holds the fp32 [64][128] pre-output tile
-constexpr uint32_t kBuf = 32768;
-constexpr uint32_t kOffBar = kOffBuf + 2 * kBuf;  // h, buf[2]
+constexpr int kPair = 2;             // chunks per CTA, stacked as the 128 rows of one MMA
+constexpr uint32_t kOffH = 0;        // h_s: 2 column blocks of [128 K rows][128 B], SW128 (MN-major B)
+constexpr uint32_t kOffQ = 32768;    // [Q''_a k0-63 | Q''_b k0-63 | Q''_a k64-127 | Q''_b k64-127] (K-major A)
+constexpr uint32_t kOffO = 65536;    // oi'' in the same arrangement
+constexpr uint32_t kOffBar = 98304;  // load, mma, TMEM slot
 constexpr uint32_t kSmem = kOffBar + 32 + 1024;
 }  // namespace sego
-
-// fp32 [64][128] tile: float4 unit u of row r sits at unit u ^ (r & 7) (conflict-free row-fragment
-// writes and 32-byte row reads)
-__device__ __forceinline__ uint32_t pre_off(int r, int c) {
-    return (uint32_t)r * 512u + ((((uint32_t)c >> 2) ^ ((uint32_t)r & 7u)) << 4) + ((uint32_t)c & 3u) * 4u;
-}
 
 __global__ void __launch_bounds__(sego::kThreads)
     gdn_prefill_seg_out_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace sego;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bar_h = reinterpret_cast<uint64_t*>(sm + kOffBar);
-    uint64_t* bar_b = bar_h + 1;
+    const uint32_t sbase = smem_u32(sm);
+    uint64_t* bar_l = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* bar_m = bar_l + 1;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_l + 2);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int gq = lane >> 2, tq = lane & 3;
     const int ss = blockIdx.x, hv = blockIdx.y;
     if (tid == 0) {
         tma_prefetch_desc(&maps.qpp);
@@ -589,111 +583,94 @@ __global__ void __launch_bounds__(sego::kThreads)
     int bos, eos;
     seq_bounds(p.cu, p.cu64, sq.n, p.T, bos, eos);
     const int seg_c0 = (ss - sq.sbase) * p.seg_m;  // first chunk of the segment (within the sequence)
-    const int c0 = seg_c0 + (int)blockIdx.z * kGroup;
-    int nch = min(kGroup, min(seg_c0 + p.seg_m, sq.nc) - c0);
+    const int c0 = seg_c0 + (int)blockIdx.z * kPair;
+    int nch = min(kPair, min(seg_c0 + p.seg_m, sq.nc) - c0);
     nch = min(nch, p.S - (sq.cbase + c0));  // only a cu_seqlens that is not non-decreasing trims it
     if (nch <= 0) return;
     if (tid == 0) {
-        mbar_init(bar_h, 1);
-        mbar_init(bar_b, 1);
-        mbar_init(bar_b + 1, 1);
+        mbar_init(bar_l, 1);
+        mbar_init(bar_m, 1);
         mbar_fence_init();
     }
+    if (warp == 0) tmem_alloc(tslot, 128);
+    tc_fence_before();
     __syncthreads();
-    auto issue = [&](int c) {  // thread 0: chunk c's Q'' and oi'' into buffer c % 2
-        unsigned char* bf = sm + kOffBuf + (c & 1) * kBuf;
-        const int row = (sq.cbase + c0 + c) * kChunk;
-        mbar_arrive_expect_tx(bar_b + (c & 1), 32768);
-        tma_load_3d(bf, &maps.qpp, 0, row, hv, bar_b + (c & 1));
-        tma_load_3d(bf + 8192, &maps.qpp, 64, row, hv, bar_b + (c & 1));
-        tma_load_3d(bf + 16384, &maps.oipp, 0, row, hv, bar_b + (c & 1));
-        tma_load_3d(bf + 24576, &maps.oipp, 64, row, hv, bar_b + (c & 1));
-    };
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
     if (tid == 0) {
-        mbar_arrive_expect_tx(bar_h, 32768);
-        tma_load_3d(sm + kOffH, &maps.seghb, 0, ss * 128, hv, bar_h);
-        tma_load_3d(sm + kOffH + 16384, &maps.seghb, 64, ss * 128, hv, bar_h);
-        issue(0);
-        if (nch > 1) issue(1);
-    }
-    bool ok = mbar_wait(bar_h, 0, p.status, kErrScanTmaTimeout);
-    // warp w: output rows 16 (w & 3) .. +15, columns 64 (w >> 2) .. +63
-    const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
-    int c = 0;
-    for (; c < nch; ++c) {
-        ok = mbar_wait(bar_b + (c & 1), (uint32_t)((c >> 1) & 1), p.status, kErrScanTmaTimeout) && ok;
-        if (!__syncthreads_and(ok)) break;
-        unsigned char* bf = sm + kOffBuf + (c & 1) * kBuf;
-        float acc[8][4];
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-#pragma unroll
-        for (int k0 = 0; k0 < 128; k0 += 16) {
-            uint32_t a[4];
-            ldsm_x4(a[0], a[1], a[2], a[3], bf + sw128_off(r0 + (lane & 15), k0 + ((lane >> 4) << 3), 8192));
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                uint32_t b0, b1, b2, b3;
-                const int kr = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
-                const int cc = n0 + 16 * np + ((lane >> 4) << 3);
-                ldsm_x4_t(b0, b1, b2, b3, sm + kOffH + sw128_off(kr, cc, 16384));
-                mma_bf16(acc[2 * np], a, b0, b1);
-                mma_bf16(acc[2 * np + 1], a, b2, b3);
-            }
+        mbar_arrive_expect_tx(bar_l, 32768 + (uint32_t)nch * 32768u);
+        tma_load_3d(sm + kOffH, &maps.seghb, 0, ss * 128, hv, bar_l);
+        tma_load_3d(sm + kOffH + 16384, &maps.seghb, 64, ss * 128, hv, bar_l);
+        for (int i = 0; i < nch; ++i) {
+            const int row = (sq.cbase + c0 + i) * kChunk;
+            tma_load_3d(sm + kOffQ + 8192 * i, &maps.qpp, 0, row, hv, bar_l);
+            tma_load_3d(sm + kOffQ + 16384 + 8192 * i, &maps.qpp, 64, row, hv, bar_l);
+            tma_load_3d(sm + kOffO + 8192 * i, &maps.oipp, 0, row, hv, bar_l);
+            tma_load_3d(sm + kOffO + 16384 + 8192 * i, &maps.oipp, 64, row, hv, bar_l);
         }
-        // + oi'' (bf16 tile in this buffer)
+    }
+    // thread (r, hf) = TMEM lane r (chunk c0 + r / 64, token row r % 64), columns 64 hf .. +63
+    const int r = lane + 32 * (warp & 3), hf = warp >> 2;
+    const int ci = r >> 6, m = r & 63;
+    const int slot = sq.cbase + c0 + ci;
+    const int t0 = bos + (c0 + ci) * kChunk;
+    const bool live = ci < nch && m < eos - t0;
+    // oi = Aqk u of the chunk (prep, column-group major [16][64][8] bf16), loaded while the MMA runs
+    uint4 oc[8];
+    if (live) {
+        const uint16_t* oi_row = p.oi + cg_off(hv, p.S, slot, 8 * hf) + m * 8;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
+        for (int g = 0; g < 8; ++g) oc[g] = *reinterpret_cast<const uint4*>(oi_row + g * 512);
+    }
+    bool ok = mbar_wait(bar_l, 0, p.status, kErrScanTmaTimeout);
+    if (tid == 0 && ok) {
+        // [Q''_a; Q''_b] (128 x 128, K-major) x h_s (128 x 128, MN-major) -> TMEM columns 0-127
+        tc_fence_after();
+        constexpr uint32_t idesc = umma_idesc_bf16(128, 128, false, true);
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int row = r0 + gq + 8 * hh, col = n0 + 8 * nt + 2 * tq;
-                const uint32_t oo = *reinterpret_cast<const uint32_t*>(bf + 16384 + sw128_off(row, col, 8192));
-                acc[nt][2 * hh] += __uint_as_float(oo << 16);
-                acc[nt][2 * hh + 1] += __uint_as_float(oo & 0xffff0000u);
-            }
-        __syncthreads();  // every warp has read Q'' and oi'': the buffer takes the fp32 tile
+        for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem, umma_desc_sw128(sbase + kOffQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+                      umma_desc_sw128(sbase + kOffH + 2048u * kk, 16384, 1024), idesc, kk > 0);
+        umma_commit(bar_m);
+    }
+    ok = __syncthreads_and(ok);
+    if (ok) ok = mbar_wait(bar_m, 0, p.status, kErrScanMmaTimeout);
+    tc_fence_after();
+    if (ok) {
+        // o = scale (Q'' h_s + oi'' + oi) for this thread's 64 columns of its token row
+        uint16_t* dst = p.out + ((size_t)(t0 + m) * p.HV + hv) * kD + 64 * hf;
+        const unsigned char* orow = sm + kOffO + (uint32_t)hf * 16384u + (uint32_t)r * 128u;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
+        for (int blk = 0; blk < 2; ++blk) {
+            uint32_t d[32];
+            tmem_ld32_async(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * hf + 32u * blk, d);
+            tmem_ld_wait();
+            tmem_regs_ready(d);
+            if (live) {
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int row = r0 + gq + 8 * hh, col = n0 + 8 * nt + 2 * tq;
-                *reinterpret_cast<float2*>(bf + pre_off(row, col)) = make_float2(acc[nt][2 * hh], acc[nt][2 * hh + 1]);
-            }
-        __syncthreads();
-        // o = scale (tile + oi), oi = Aqk u of the chunk (prep, column-group major [16][64][8] bf16);
-        // thread = (row, 8-column group): 16-byte loads and stores
-        {
-            const int slot = sq.cbase + c0 + c;
-            const int t0 = bos + (c0 + c) * kChunk;
-            const int L = min(kChunk, eos - t0);
-            const uint16_t* oi_slot = p.oi + cg_off(hv, p.S, slot, 0);
-#pragma unroll
-            for (int it = 0; it < 4; ++it) {
-                const int idx = tid + 256 * it, row = idx >> 4, cg = idx & 15;
-                if (row < L) {
-                    const float4 x0 = *reinterpret_cast<const float4*>(bf + pre_off(row, 8 * cg));
-                    const float4 x1 = *reinterpret_cast<const float4*>(bf + pre_off(row, 8 * cg + 4));
-                    const uint4 oc = *reinterpret_cast<const uint4*>(oi_slot + cg * 512 + row * 8);
-                    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                    const uint32_t ow[4] = {oc.x, oc.y, oc.z, oc.w};
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    const int g = 4 * blk + q4;
+                    const uint4 o2 = *reinterpret_cast<const uint4*>(orow + ((g ^ (r & 7)) << 4));
+                    const uint32_t pw[4] = {o2.x, o2.y, o2.z, o2.w};
+                    const uint32_t ow[4] = {oc[g].x, oc[g].y, oc[g].z, oc[g].w};
                     uint32_t pk[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        pk[e] = pack_bf16x2(p.scale * (xs[2 * e] + __uint_as_float(ow[e] << 16)),
-                                            p.scale * (xs[2 * e + 1] + __uint_as_float(ow[e] & 0xffff0000u)));
-                    *reinterpret_cast<uint4*>(p.out + ((size_t)(t0 + row) * p.HV + hv) * kD + 8 * cg) =
-                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 x2 = add2(add2(make_float2(__uint_as_float(d[8 * q4 + 2 * e]), __uint_as_float(d[8 * q4 + 2 * e + 1])),
+                                                    make_float2(__uint_as_float(pw[e] << 16), __uint_as_float(pw[e] & 0xffff0000u))),
+                                               make_float2(__uint_as_float(ow[e] << 16), __uint_as_float(ow[e] & 0xffff0000u)));
+                        pk[e] = pack_bf16x2(p.scale * x2.x, p.scale * x2.y);
+                    }
+                    *reinterpret_cast<uint4*>(dst + 8 * g) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
             }
         }
-        fence_async_smem();  // this thread's accesses to the buffer come before the next TMA write
-        __syncthreads();     // the buffer is free: chunk c + 2 may load into it
-        if (tid == 0 && c + 2 < nch) issue(c + 2);
+    } else if (tid == 0) {
+        mbar_wait(bar_l, 0, nullptr, 0);  // let copies in flight land (bounded) before the CTA exits
     }
-    if (c < nch && tid == 0)  // gave up: let copies in flight land (bounded) before the CTA exits
-        for (int cc = c; cc < min(nch, c + 2); ++cc) mbar_wait(bar_b + (cc & 1), (uint32_t)((cc >> 1) & 1), nullptr, 0);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
 int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream) {
@@ -713,7 +690,7 @@ int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream
                    stream, p, maps) != cudaSuccess)
         return -1;
     if (launch_pdl(gdn_prefill_seg_out_kernel,
-                   dim3((unsigned)std::max<long long>(segs, 1), p.HV, (p.seg_m + sego::kGroup - 1) / sego::kGroup),
+                   dim3((unsigned)std::max<long long>(segs, 1), p.HV, (p.seg_m + sego::kPair - 1) / sego::kPair),
                    dim3(sego::kThreads), sego::kSmem, stream, p, maps) != cudaSuccess)
         return -1;
     return 0;
