@@ -164,10 +164,13 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     const unsigned forced_bv = (flags >> 8) & 0xffu;
     const int bv = forced_bv ? (int)forced_bv : gdn::prefill_scan_bv(N, HV);
     if (bv != 8 && bv != 16 && bv != 32 && bv != 64) return GDN_ERR_SIZE;
-    // Segmented route: the default whenever the layout has its regions, unless a scan variant is
-    // forced or GDN_FLAG_NO_SEGMENTS is set; bits 16-23 force the segment length (it must not
-    // need more segment slots than the layout holds).
-    p.seg_m = (forced_bv || (flags & GDN_FLAG_NO_SEGMENTS)) ? 0 : lay.seg_m;
+    // Segmented route (only when the layout has its regions): the default for a few sequences
+    // averaging >= 6144 tokens, or forced by GDN_FLAG_SEGMENTS; never with a forced scan variant or
+    // GDN_FLAG_NO_SEGMENTS.  Bits 16-23 force its segment length, which must not need more segment
+    // slots than the layout holds.
+    const bool seg_on = ((flags & GDN_FLAG_SEGMENTS) || gdn::prefill_seg_default(N, T)) && !forced_bv &&
+                        !(flags & GDN_FLAG_NO_SEGMENTS);
+    p.seg_m = seg_on ? lay.seg_m : 0;
     p.SS = lay.SS;
     const unsigned forced_m = (flags >> 16) & 0xffu;
     if (p.seg_m > 0 && forced_m) {

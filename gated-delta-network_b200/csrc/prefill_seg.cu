@@ -38,8 +38,9 @@ GDN_DBG_READER(gdn_debug_read_seg)
 namespace gdn {
 
 namespace segk {
-constexpr int kThreads = 288;  // 8 math warps (two per TMEM lane quarter) + 1 TMA producer warp
-constexpr int kMath = 256;
+constexpr int kThreads = 544;  // 16 math warps (four per TMEM lane quarter) + 1 TMA producer warp
+constexpr int kMath = 512;
+constexpr int kCW = 32;        // state columns per math thread
 constexpr int kStages = 2;
 constexpr uint32_t kOffWQ = 0;          // [W0 | Q'0 | W1 | Q'1], 8 KB each; after MMA_P: output staging
 constexpr uint32_t kOffK = 32768;       // k tile, 2 atoms of 64 tokens x 128 B
@@ -97,12 +98,13 @@ __device__ __forceinline__ SegSeq warp_seg_seq(const PrefillArgs& p, int kind, i
     return r;
 }
 
-// bf16 copy of X row r, columns 64 hf .. +63: MN-major SW128 B operand of MMA_P, column block hf
+// bf16 copy of X row r, columns cb .. cb + kCW - 1: MN-major SW128 B operand of MMA_P (column
+// block bk, 16-byte chunks j0 ..)
 #define GDN_SEG_WRITE_XB()                                                                                     \
     do {                                                                                                      \
-        unsigned char* row_ = sm + kOffX + hf * 16384 + r * 128;                                               \
-        _Pragma("unroll") for (int jj = 0; jj < 8; ++jj)                                                      \
-            *reinterpret_cast<uint4*>(row_ + ((jj ^ (r & 7)) << 4)) =                                          \
+        unsigned char* row_ = sm + kOffX + bk * 16384 + r * 128;                                               \
+        _Pragma("unroll") for (int jj = 0; jj < kCW / 8; ++jj)                                                \
+            *reinterpret_cast<uint4*>(row_ + (((j0 + jj) ^ (r & 7)) << 4)) =                                   \
                 make_uint4(pack_bf16x2(x[8 * jj], x[8 * jj + 1]), pack_bf16x2(x[8 * jj + 2], x[8 * jj + 3]),   \
                            pack_bf16x2(x[8 * jj + 4], x[8 * jj + 5]), pack_bf16x2(x[8 * jj + 6], x[8 * jj + 7])); \
     } while (0)
@@ -110,8 +112,8 @@ __device__ __forceinline__ SegSeq warp_seg_seq(const PrefillArgs& p, int kind, i
 // ------------------------------------------------------------------------------------------
 // 1. local transitions
 // ------------------------------------------------------------------------------------------
-// 288 threads: registers are granted to warps in groups of four, so 12 warps' worth of the
-// 64 K-entry file caps this kernel at 168 registers per thread
+// 544 threads: registers are granted to warps in groups of four, so 20 warps' worth of the
+// 64 K-entry file caps this kernel at 96 registers per thread
 __global__ void __launch_bounds__(segk::kThreads, 1)
     gdn_prefill_seg_local_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace segk;
@@ -186,13 +188,14 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
             }
         }
     } else {
-        // ---- math warps: thread (r, hf) = TMEM lane r, state columns 64 hf .. 64 hf + 63 ----
-        const int r = lane + 32 * (warp & 3), hf = warp >> 2;
-        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * hf;
-        float x[64];  // X row r (K index), columns 64 hf + j
+        // ---- math warps: thread (r, cq) = TMEM lane r, state columns cb = kCW cq .. cb + kCW - 1 ----
+        // (warps w, w + 4, w + 8, w + 12 share TMEM lane quarter w and split its columns)
+        const int r = lane + 32 * (warp & 3), cq = warp >> 2;
+        const int cb = kCW * cq, bk = cb >> 6, j0 = (cb & 63) >> 3;
+        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)cb;
+        float x[kCW];  // X row r (K index), columns cb + j
 #pragma unroll
-        for (int j = 0; j < 64; ++j) x[j] = (half == 1 && r == 64 * hf + j) ? 1.f : 0.f;
-        // bf16 copy of X: MN-major SW128 B operand of MMA_P, column block hf, row r
+        for (int j = 0; j < kCW; ++j) x[j] = (half == 1 && r == cb + j) ? 1.f : 0.f;
         GDN_SEG_WRITE_XB();
         constexpr uint32_t idesc_p = umma_idesc_bf16(128, 128, false, true);
         constexpr uint32_t idesc_u = umma_idesc_bf16(128, 128, true, true);
@@ -241,11 +244,11 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                 const float4 g4r = *reinterpret_cast<const float4*>(G4 + r * 4);  // {G, e^G, beta, rk}
                 const float ed = __expf(GL - g4r.x) * g4r.w;
                 const float* Us = reinterpret_cast<const float*>(st + kOffU);
-                unsigned char* rh = sm + kOffX + hf * 8192 + r * 128;
+                unsigned char* rh = sm + kOffX + bk * 8192 + r * 128;
                 unsigned char* rl = rh + 16384;
                 const int hA = (r >> 2) & 1;
 #pragma unroll
-                for (int blk = 0; blk < 2; ++blk) {
+                for (int blk = 0; blk < kCW / 32; ++blk) {
                     uint32_t d[32];
                     if (zeroP) {
 #pragma unroll
@@ -255,12 +258,13 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                         tmem_ld_wait();
                         tmem_regs_ready(d);
                     }
+                    GDN_PH_ACC(dbg, 8 + 2 * blk, tp);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int jj = 4 * blk + q4;  // 8-column group inside this thread's 64 columns
                         float uu[8];
                         if (half == 0) {
-                            const int cg = 8 * hf + jj;
+                            const int cg = (cb >> 3) + jj;
                             const float4 x0 = *reinterpret_cast<const float4*>(Us + (cg * 64 + r) * 8 + 4 * hA);
                             const float4 x1 = *reinterpret_cast<const float4*>(Us + (cg * 64 + r) * 8 + 4 * (hA ^ 1));
                             const float4 ua = hA ? x1 : x0;
@@ -283,15 +287,16 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                                                                    __uint_as_float(hi[e] & 0xffff0000u)));
                             lo[e] = pack_bf16x2(r2.x, r2.y);
                         }
-                        *reinterpret_cast<uint4*>(rh + ((jj ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4*>(rl + ((jj ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4*>(rh + (((j0 + jj) ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(rl + (((j0 + jj) ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
+                    GDN_PH_ACC(dbg, 9 + 2 * blk, tp);
                 }
                 // warps 0, 1, 4, 5 alone gate MMA_U
                 GDN_PH_ACC(dbg, 3, tp);
                 fence_async_smem();
                 tc_fence_before();
-                okv = named_bar_and(2, 128, ok && okv);
+                okv = named_bar_and(2, kMath / 2, ok && okv);
                 tc_fence_after();
                 GDN_PH_ACC(dbg, 4, tp);
                 // MMA_U: K^T (128 x 64 tokens, MN-major) x (vn_hi + vn_lo) -> TMEM columns 128-255
@@ -311,9 +316,9 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                 // output operand row m = r - 64: oi'' = Q' beta (half 0) or Q'' = Q' Phi (half 1),
                 // staged SW128 in the stage's (consumed) W / Q' area, then one TMA store per 64 columns
                 const int m = r - 64;
-                unsigned char* orow = sm + (c % kStages) * kStage + kOffWQ + hf * 8192 + m * 128;
+                unsigned char* orow = sm + (c % kStages) * kStage + kOffWQ + bk * 8192 + m * 128;
 #pragma unroll
-                for (int blk = 0; blk < 2; ++blk) {
+                for (int blk = 0; blk < kCW / 32; ++blk) {
                     uint32_t d[32];
                     if (zeroP) {
 #pragma unroll
@@ -330,11 +335,11 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
 #pragma unroll
                         for (int e = 0; e < 4; ++e)
                             pk[e] = pack_bf16x2(__uint_as_float(d[8 * q4 + 2 * e]), __uint_as_float(d[8 * q4 + 2 * e + 1]));
-                        *reinterpret_cast<uint4*>(orow + ((jj ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        *reinterpret_cast<uint4*>(orow + (((j0 + jj) ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     }
                 }
                 fence_async_smem();
-                named_bar_sync(3, 128);  // the four output warps
+                named_bar_sync(3, kMath / 2);  // the output warps
                 if (tid == 64) {         // warp 2, lane 0: store the 64 x 128 tile (two SW128 boxes)
                     unsigned char* ob = sm + (c % kStages) * kStage + kOffWQ;
                     tma_store_3d(omap, 0, slot * kChunk, hv, ob);
@@ -350,7 +355,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
             {
                 const float eL = __expf(GL);
 #pragma unroll
-                for (int blk = 0; blk < 2; ++blk) {
+                for (int blk = 0; blk < kCW / 32; ++blk) {
                     uint32_t d[32];
                     tmem_ld32_async(tl + 128u + 32u * blk, d);
                     tmem_ld_wait();
@@ -384,19 +389,19 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                 // B = beta_end, column-group major [16][128][8] f32
                 float* Bp = p.seg_B + seg_i * 128 * 128;
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    float4* dst = reinterpret_cast<float4*>(Bp + ((8 * hf + jj) * 128 + r) * 8);
+                for (int jj = 0; jj < kCW / 8; ++jj) {
+                    float4* dst = reinterpret_cast<float4*>(Bp + (((cb >> 3) + jj) * 128 + r) * 8);
                     dst[0] = make_float4(x[8 * jj], x[8 * jj + 1], x[8 * jj + 2], x[8 * jj + 3]);
                     dst[1] = make_float4(x[8 * jj + 4], x[8 * jj + 5], x[8 * jj + 6], x[8 * jj + 7]);
                 }
             } else {
                 // D = Phi_end - gamma I, row-major [128][128] bf16 (row = output k index)
 #pragma unroll
-                for (int j = 0; j < 64; ++j)
-                    if (r == 64 * hf + j) x[j] -= gamma;
-                uint4* dst = reinterpret_cast<uint4*>(p.seg_D + (seg_i * 128 + r) * 128 + 64 * hf);
+                for (int j = 0; j < kCW; ++j)
+                    if (r == cb + j) x[j] -= gamma;
+                uint4* dst = reinterpret_cast<uint4*>(p.seg_D + (seg_i * 128 + r) * 128 + cb);
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj)
+                for (int jj = 0; jj < kCW / 8; ++jj)
                     dst[jj] = make_uint4(pack_bf16x2(x[8 * jj], x[8 * jj + 1]), pack_bf16x2(x[8 * jj + 2], x[8 * jj + 3]),
                                          pack_bf16x2(x[8 * jj + 4], x[8 * jj + 5]), pack_bf16x2(x[8 * jj + 6], x[8 * jj + 7]));
                 if (tid == 0) p.seg_gamma[seg_i] = gamma;

@@ -1,7 +1,7 @@
 """The segmented prefill route (csrc/prefill_seg.cu) against the CPU oracle and against the
-single-pass scan.  Calls of few long sequences take it by default (gdn_prefill_fwd picks the
-segment length from N and T); GDN_FLAG_NO_SEGMENTS forces the single-pass scan, and bits 16-23
-force a segment length.  Cases cover one sequence, several, ragged tails, a one-token and a
+single-pass scan.  Calls of a few sequences averaging >= 6144 tokens take it by default;
+GDN_FLAG_SEGMENTS forces it for the other calls whose workspace has its regions,
+GDN_FLAG_NO_SEGMENTS forces the single-pass scan, and bits 16-23 force a segment length.  Cases cover one sequence, several, ragged tails, a one-token and a
 zero-length sequence, and segment lengths that do and do not divide the chunk count."""
 import numpy as np
 import pytest
@@ -16,6 +16,7 @@ from tests.golden import inputs as gi
 pytestmark = pytest.mark.gpu
 
 NO_SEGMENTS = 0x8
+SEGMENTS = 0x10
 
 
 def _call(inp, flags=0):
@@ -45,7 +46,7 @@ CASES = [
 @pytest.mark.parametrize("lens,with_state", CASES, ids=["-".join(map(str, l)) for l, _ in CASES])
 def test_segmented_prefill_matches_oracle(lens, with_state):
     inp = gi.prefill_inputs(lens, seed=1000 + sum(lens), with_state=with_state)
-    out, ns = _call(inp)
+    out, ns = _call(inp, SEGMENTS)
     ro, rs = _oracle(inp)
     util.check_out(util.bits(out), ro)
     util.check_state(ns.cpu().numpy(), rs)
@@ -61,7 +62,7 @@ def test_segmented_prefill_forced_segment_lengths(m):
     segment) give the oracle's results.  Shorter ones would need more segment slots than the
     workspace holds (GDN_ERR_SIZE, checked below)."""
     inp = gi.prefill_inputs([4096], seed=77, with_state=True)
-    out, ns = _call(inp, m << 16)
+    out, ns = _call(inp, SEGMENTS | (m << 16))
     ro, rs = _oracle(inp)
     util.check_out(util.bits(out), ro)
     util.check_state(ns.cpu().numpy(), rs)
@@ -72,7 +73,7 @@ def test_segmented_prefill_weak_decay_long_memory():
     segment transitions, which then carry most of the state across segments."""
     inp = gi.prefill_inputs([4096], seed=78, with_state=True)
     inp["A_log"] = np.full(8, -6.0, np.float32)
-    out, ns = _call(inp)
+    out, ns = _call(inp, SEGMENTS)
     out1, ns1 = _call(inp, NO_SEGMENTS)
     ro, rs = _oracle(inp)
     util.check_out(util.bits(out), ro)
@@ -84,12 +85,13 @@ def test_segmented_prefill_weak_decay_long_memory():
 
 
 def test_segmented_prefill_in_place_and_graph_capture():
-    """new_state aliasing state (destination-passing, in place) and replay from a CUDA graph."""
-    inp = gi.prefill_inputs([2048, 1500], seed=79, with_state=True)
+    """new_state aliasing state (destination-passing, in place) and replay from a CUDA graph, on
+    the default route of two long sequences (segmented)."""
+    inp = gi.prefill_inputs([6400, 7000], seed=79, with_state=True)
     ro, rs = _oracle(inp)
     args = list(util.prefill_args(inp))
     st = args[3]
-    out = torch.empty(3548, 8, 128, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(13400, 8, 128, dtype=torch.bfloat16, device="cuda")
     g = torch.cuda.CUDAGraph()
     s0 = st.clone()
     side = torch.cuda.Stream()
@@ -114,5 +116,14 @@ def test_segmented_prefill_in_place_and_graph_capture():
 def test_segmented_prefill_rejects_segments_beyond_the_workspace():
     inp = gi.prefill_inputs([4096], seed=80, with_state=True)
     with pytest.raises(gdn.GDNError) as e:
-        _call(inp, 2 << 16)
+        _call(inp, SEGMENTS | (2 << 16))
     assert e.value.status == 4  # GDN_ERR_SIZE
+
+
+def test_segmented_route_is_the_default_for_long_sequences():
+    """Default flags on a 1 x 8192 call give the same bits as forcing the segmented route."""
+    inp = gi.prefill_inputs([8192], seed=81, with_state=True)
+    o1, s1 = _call(inp)
+    o2, s2 = _call(inp, SEGMENTS)
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+    assert torch.equal(s1.view(torch.int32), s2.view(torch.int32))
