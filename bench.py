@@ -447,22 +447,26 @@ def main():
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     from gdn import prefill as pmod
 
-    def prefill_step():
-        pmod._launch(pq, pk, pv, ph0, A_log, pa, dt_bias, pb, cu, scale, pout, pns, workspace=ws)
+    def prefill_step(flags=0):
+        pmod._launch(pq, pk, pv, ph0, A_log, pa, dt_bias, pb, cu, scale, pout, pns, workspace=ws, flags=flags)
 
-    for _ in range(args.warmup):
-        prefill_step()
-    barrier()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.prefill_steps)]
-    for e0, e1 in evs:
-        flush.fill_(1)
-        e0.record()
-        prefill_step()
-        e1.record()
-    barrier()
-    pre_ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
-    pre_ms = max_over_ranks(pre_ms)
+    def time_8k(flags):
+        for _ in range(args.warmup):
+            prefill_step(flags)
+        barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.prefill_steps)]
+        for e0, e1 in evs:
+            flush.fill_(1)
+            torch.cuda._sleep(200_000)  # keeps the GPU busy while the host submits the call
+            e0.record()
+            prefill_step(flags)
+            e1.record()
+        barrier()
+        return max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs))
+
+    pre_ms = time_8k(0)  # the library's default route (segmented for one 8192-token sequence)
+    pre_routes = {"segmented_ms": round(time_8k(0x10), 5), "single_pass_scan_ms": round(time_8k(0x8), 5)}
 
     # ---------------- other prefill configurations (reported alongside) ----------------
     def time_prefill(lens, with_state, steps=10):
@@ -485,6 +489,7 @@ def main():
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         for e0, e1 in evs:
             flush.fill_(1)
+            torch.cuda._sleep(200_000)  # keeps the GPU busy while the host submits the call
             e0.record()
             step()
             e1.record()
@@ -715,6 +720,7 @@ def main():
             "roofline": {"bound": "max(hbm, tensor)", "achieved_frac": round(pre_bound_s / (pre_ms * 1e-3), 5),
                          "bound_us": round(pre_bound_s * 1e6, 3), "alg_bytes": pre_bytes, "alg_flops": pre_flops,
                          "traffic": NCU_TRAFFIC["prefill_scan"], "peak_source": peak_src},
+            "routes": pre_routes,
             "e2e": pre_e2e,
         },
         "prefill_configs": prefill_more,

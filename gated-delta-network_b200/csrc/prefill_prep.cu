@@ -619,8 +619,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                               umma_desc_sw128(sbase + kOffK0 + 2048u * kk, kOffK1 - kOffK0, 1024), idesc, kk > 0);
                 umma_commit(bar_mma);
             }
+            // (the w / u stores keep reading the K tile and the u staging while epilogue #3 runs: it
+            // writes Q' into the Q tile and oi into MMA #3's consumed A operand)
             ok = mbar_wait(bar_mma, ph, p.status, kErrPrepMmaTimeout);
-            if (tid == 0) tma_store_wait_read();  // the w store has read the K tile: it can be overwritten
             ok = __syncthreads_and(ok);
             if (!ok) goto cleanup;
             tc_fence_after();
@@ -632,7 +633,8 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                 const uint32_t tl = tmem + ((uint32_t)(32 * wq) << 16);
                 const int m = r & 63;
                 const float eg = Es[m] * Rq[m];
-                // Q' -> K tile (SW128, TMA store); oi -> staging [16][64][8] bf16 in the (read) u staging area
+                // Q' -> the Q tile in place (each thread reads its q chunk, then writes Q' there; SW128,
+                // TMA store); oi -> staging [16][64][8] bf16 in the [Aqk; Aqk] operand area (MMA #3 is done)
                 tmem_two_blocks(tl + (r < 64 ? 0 : 128) + 64 * ch_half, 2 * ch_half, [&](int cb, const uint32_t(&dr)[32]) {
                     const float* d = reinterpret_cast<const float*>(dr);
 #pragma unroll
@@ -654,9 +656,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                         const uint4 x4 = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
                                                     pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
                         if (r < 64)
-                            *reinterpret_cast<uint4*>(sm + kOffK0 + sw128_off(m, c, kOffK1 - kOffK0)) = x4;
+                            *reinterpret_cast<uint4*>(sm + kOffQ0 + sw128_off(m, c, kOffQ1 - kOffQ0)) = x4;
                         else
-                            *reinterpret_cast<uint4*>(sm + kOffA + ((c >> 3) * 64 + m) * 16) = x4;
+                            *reinterpret_cast<uint4*>(sm + kOffAq + ((c >> 3) * 64 + m) * 16) = x4;
                     }
                 });
             }
@@ -666,9 +668,9 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
             GDN_PH_ACC(dbg, 15, tp);
             if (tid == 0) {
                 const int wr = slot * kChunk;
-                tma_store_3d(&maps.qp, 0, wr, hv, sm + kOffK0);
-                tma_store_3d(&maps.qp, 64, wr, hv, sm + kOffK1);
-                bulk_store(p.oi + cg_off(hv, p.S, slot, 0), sm + kOffA, 16 * 64 * 8 * 2);
+                tma_store_3d(&maps.qp, 0, wr, hv, sm + kOffQ0);
+                tma_store_3d(&maps.qp, 64, wr, hv, sm + kOffQ1);
+                bulk_store(p.oi + cg_off(hv, p.S, slot, 0), sm + kOffAq, 16 * 64 * 8 * 2);
                 tma_store_commit();
             }
 
