@@ -248,20 +248,20 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                 unsigned char* rl = rh + 16384;
                 const int hA = (r >> 2) & 1;
 #pragma unroll
-                for (int blk = 0; blk < kCW / 32; ++blk) {
-                    uint32_t d[32];
+                for (int blk = 0; blk < kCW / 16; ++blk) {
+                    uint32_t d[16];
                     if (zeroP) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) d[j] = 0u;
+                        for (int j = 0; j < 16; ++j) d[j] = 0u;
                     } else {
-                        tmem_ld32_async(tl + 32u * blk, d);
+                        tmem_ld16_async(tl + 16u * blk, d);
                         tmem_ld_wait();
-                        tmem_regs_ready(d);
+                        tmem_regs_ready_n(d);
                     }
-                    GDN_PH_ACC(dbg, 8 + 2 * blk, tp);
+                    GDN_PH_ACC(dbg, 8 + 2 * (blk & 1), tp);
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        const int jj = 4 * blk + q4;  // 8-column group inside this thread's 64 columns
+                    for (int q4 = 0; q4 < 2; ++q4) {
+                        const int jj = 2 * blk + q4;  // 8-column group inside this thread's columns
                         float uu[8];
                         if (half == 0) {
                             const int cg = (cb >> 3) + jj;
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                         *reinterpret_cast<uint4*>(rh + (((j0 + jj) ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                         *reinterpret_cast<uint4*>(rl + (((j0 + jj) ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
-                    GDN_PH_ACC(dbg, 9 + 2 * blk, tp);
+                    GDN_PH_ACC(dbg, 9 + 2 * (blk & 1), tp);
                 }
                 // warps 0, 1, 4, 5 alone gate MMA_U
                 GDN_PH_ACC(dbg, 3, tp);
@@ -318,19 +318,19 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
                 const int m = r - 64;
                 unsigned char* orow = sm + (c % kStages) * kStage + kOffWQ + bk * 8192 + m * 128;
 #pragma unroll
-                for (int blk = 0; blk < kCW / 32; ++blk) {
-                    uint32_t d[32];
+                for (int blk = 0; blk < kCW / 16; ++blk) {
+                    uint32_t d[16];
                     if (zeroP) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) d[j] = 0u;
+                        for (int j = 0; j < 16; ++j) d[j] = 0u;
                     } else {
-                        tmem_ld32_async(tl + 32u * blk, d);
+                        tmem_ld16_async(tl + 16u * blk, d);
                         tmem_ld_wait();
-                        tmem_regs_ready(d);
+                        tmem_regs_ready_n(d);
                     }
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        const int jj = 4 * blk + q4;
+                    for (int q4 = 0; q4 < 2; ++q4) {
+                        const int jj = 2 * blk + q4;
                         uint32_t pk[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e)
@@ -355,17 +355,17 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
             {
                 const float eL = __expf(GL);
 #pragma unroll
-                for (int blk = 0; blk < kCW / 32; ++blk) {
-                    uint32_t d[32];
-                    tmem_ld32_async(tl + 128u + 32u * blk, d);
+                for (int blk = 0; blk < kCW / 16; ++blk) {
+                    uint32_t d[16];
+                    tmem_ld16_async(tl + 128u + 16u * blk, d);
                     tmem_ld_wait();
-                    tmem_regs_ready(d);
+                    tmem_regs_ready_n(d);
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        const float2 xn = fma2(make_float2(eL, eL), make_float2(x[32 * blk + j], x[32 * blk + j + 1]),
+                    for (int j = 0; j < 16; j += 2) {
+                        const float2 xn = fma2(make_float2(eL, eL), make_float2(x[16 * blk + j], x[16 * blk + j + 1]),
                                                make_float2(__uint_as_float(d[j]), __uint_as_float(d[j + 1])));
-                        x[32 * blk + j] = xn.x;
-                        x[32 * blk + j + 1] = xn.y;
+                        x[16 * blk + j] = xn.x;
+                        x[16 * blk + j + 1] = xn.y;
                     }
                 }
                 gamma *= eL;
