@@ -253,6 +253,44 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def profile_run(args):
+    """A few calls of one prefill or decode configuration with the benchmark's input distributions,
+    nothing timed: the command that the ncu summaries under profiles/ capture."""
+    import torch
+
+    import gdn
+    from gdn import prefill as pmod
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    rn = lambda *sh: torch.randn(*sh, generator=g, device=dev)
+    l2n = lambda x: (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    A_log = torch.rand(HV, generator=g, device=dev) * math.log(16.0)
+    dt_bias = rn(HV) * 0.1
+    if args.profile_decode:
+        B = args.profile_decode
+        q, k = l2n(rn(B, 1, H, D)), l2n(rn(B, 1, H, D))
+        v, a, b = rn(B, 1, HV, D).bfloat16(), rn(B, 1, HV).bfloat16(), rn(B, 1, HV).bfloat16()
+        st = rn(B, HV, D, D) * 0.02
+        out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            gdn.decode.kernel(q, k, v, st, A_log, a, dt_bias, b, D ** -0.5, out, st)
+    else:
+        parts = [int(x, 0) for x in args.profile_prefill.split(",")]
+        N, T, flags = parts[0], parts[1], (parts[2] if len(parts) > 2 else 0)
+        TT = N * T
+        q, k = l2n(rn(TT, H, D)), l2n(rn(TT, H, D))
+        v, a, b = rn(TT, HV, D).bfloat16(), rn(TT, HV).bfloat16(), rn(TT, HV).bfloat16()
+        h0 = rn(N, HV, D, D) * 0.02
+        cu = torch.arange(N + 1, dtype=torch.int32, device=dev) * T
+        out = torch.empty(TT, HV, D, dtype=torch.bfloat16, device=dev)
+        ns = torch.empty(N, HV, D, D, device=dev)
+        ws = torch.empty(gdn.prefill.workspace_bytes(N, TT), dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            pmod._launch(q, k, v, h0, A_log, a, dt_bias, b, cu, D ** -0.5, out, ns, workspace=ws, flags=flags)
+    torch.cuda.synchronize()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -263,6 +301,11 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-prefill", metavar="N,T[,FLAGS]", default=None,
+                    help="profiling aid (ncu): run 3 prefill calls of N sequences x T tokens (library flags, "
+                         "e.g. 0x8 for the single-pass scan) and exit; prints no JSON line")
+    ap.add_argument("--profile-decode", metavar="B", type=int, default=None,
+                    help="profiling aid (ncu): run 3 decode steps at batch B and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -272,6 +315,9 @@ def main():
 
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.profile_prefill or args.profile_decode:
+        profile_run(args)
         return
 
     import torch
