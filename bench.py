@@ -55,9 +55,11 @@ PREFILL_FLOPS_PER_TOKEN = (10 * 64 * 128 + 6 * 128 * 128) * HV                  
 N_STATE_BUFS = 8
 REPS = 5  # timed repetitions of every measurement; the median is reported
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum), or None.
-# Source: the ncu summaries under profiles/ (decode B=64 launch; prefill kernels at T=8192).
+# Source: the ncu summaries under profiles/ (decode B=64 launch; prefill at T=8192).
 # decode: 33.83 MB read; the 33.55 MB of state writes are still dirty in L2 when ncu's replayed launch ends.
-NCU_TRAFFIC = {"decode": 33832960, "prefill_scan": 100973312}
+# prefill_8k_call: the four launches of one default-route call (prep 59.9 MB, segment-local 87.0, chain 7.6,
+# output 52.8), each measured with ncu's per-kernel cache flush.
+NCU_TRAFFIC = {"decode": 33832960, "prefill_8k_call": 207338155}
 
 
 def env_int(name, default):
@@ -765,7 +767,8 @@ def main():
             "config": "one 8192-token sequence per GPU, cu_seqlens int32, initial state N(0,0.02); L2 flushed",
             "roofline": {"bound": "max(hbm, tensor)", "achieved_frac": round(pre_bound_s / (pre_ms * 1e-3), 5),
                          "bound_us": round(pre_bound_s * 1e6, 3), "alg_bytes": pre_bytes, "alg_flops": pre_flops,
-                         "traffic": NCU_TRAFFIC["prefill_scan"], "peak_source": peak_src},
+                         "traffic": NCU_TRAFFIC["prefill_8k_call"], "traffic_scope": "all kernels of one call",
+                         "peak_source": peak_src},
             "routes": pre_routes,
             "e2e": pre_e2e,
         },
