@@ -19,7 +19,7 @@
 //   2. gdn_prefill_seg_chain_kernel, one CTA per (8 state columns, sequence, v-head): the short
 //      serial chain over segments, h_{s+1} = gamma h_s + D h_s + B; it records each h_s (bf16,
 //      the output operand) and writes the final state.
-//   3. gdn_prefill_seg_out_kernel, one CTA per (2 chunks of a segment, v-head), one tcgen05 MMA:
+//   3. gdn_prefill_seg_out_kernel, persistent, one tcgen05 MMA per (2 chunks of a segment, v-head):
 //      o_j = scale (Q''_j h_s + oi''_j + oi_j), oi_j = Aqk u from the prep.
 //
 // Per chunk the local kernel does what the single-pass scan does (two dependent products), on a
@@ -555,113 +555,182 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
 // 3. outputs
 // ------------------------------------------------------------------------------------------
 namespace sego {
-constexpr int kThreads = 256;
-constexpr int kPair = 2;             // chunks per CTA, stacked as the 128 rows of one MMA
+// Persistent: one CTA per SM walks (segment, v-head, pair of chunks) items.  Warps 0-7 run the
+// epilogues, warp 8 issues the TMA loads, warp 9 the MMAs; operands and TMEM accumulators are double
+// buffered, so one item's loads and product overlap the previous item's epilogue.
+constexpr int kThreads = 320;
+constexpr int kEpi = 256;
+constexpr int kProdWarp = 8, kMmaWarp = 9;
+constexpr int kPair = 2;             // chunks per item, stacked as the 128 rows of one MMA
+constexpr uint32_t kBuf = 98304;     // per buffer: h_s, [Q''_a | Q''_b] (K-major A), oi'' (same arrangement)
 constexpr uint32_t kOffH = 0;        // h_s: 2 column blocks of [128 K rows][128 B], SW128 (MN-major B)
-constexpr uint32_t kOffQ = 32768;    // [Q''_a k0-63 | Q''_b k0-63 | Q''_a k64-127 | Q''_b k64-127] (K-major A)
-constexpr uint32_t kOffO = 65536;    // oi'' in the same arrangement
-constexpr uint32_t kOffBar = 98304;  // load, mma, TMEM slot
-constexpr uint32_t kSmem = kOffBar + 32 + 1024;
+constexpr uint32_t kOffQ = 32768;    // [Q''_a k0-63 | Q''_b k0-63 | Q''_a k64-127 | Q''_b k64-127]
+constexpr uint32_t kOffO = 65536;
+constexpr uint32_t kOffBar = 2 * kBuf;  // full[2], empty[2], mfull[2], accfree[2], TMEM slot
+constexpr uint32_t kSmem = kOffBar + 8 * 8 + 16 + 1024;
 }  // namespace sego
 
-__global__ void __launch_bounds__(sego::kThreads)
+// Item w -> (segment slot, v-head, pair); false when the item holds no chunk.  Warp-wide (every lane
+// of the calling warp gets the same answer), so every role walks the same sequence of items.
+struct OutItem {
+    int ss, hv, slot, t0, L0, L1, nch;
+};
+__device__ __forceinline__ bool seg_out_item(const PrefillArgs& p, int w, int npair, OutItem& it) {
+    const int z = w % npair, hv = (w / npair) % p.HV, ss = w / (npair * p.HV);
+    if (ss >= p.SS) return false;
+    const SegSeq sq = warp_seg_seq(p, kBySeg, ss);
+    if (sq.n < 0) return false;
+    int bos, eos;
+    seq_bounds(p.cu, p.cu64, sq.n, p.T, bos, eos);
+    const int seg_c0 = (ss - sq.sbase) * p.seg_m;
+    const int c0 = seg_c0 + z * sego::kPair;
+    int nch = min(sego::kPair, min(seg_c0 + p.seg_m, sq.nc) - c0);
+    nch = min(nch, p.S - (sq.cbase + c0));  // only a cu_seqlens that is not non-decreasing trims it
+    if (nch <= 0) return false;
+    it.ss = ss;
+    it.hv = hv;
+    it.slot = sq.cbase + c0;
+    it.t0 = bos + c0 * kChunk;
+    it.L0 = min(kChunk, eos - it.t0);
+    it.L1 = nch > 1 ? min(kChunk, eos - it.t0 - kChunk) : 0;
+    it.nch = nch;
+    return true;
+}
+
+__global__ void __launch_bounds__(sego::kThreads, 1)
     gdn_prefill_seg_out_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace sego;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(sm);
-    uint64_t* bar_l = reinterpret_cast<uint64_t*>(sm + kOffBar);
-    uint64_t* bar_m = bar_l + 1;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_l + 2);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* empty = full + 2;
+    uint64_t* mfull = full + 4;
+    uint64_t* accfree = full + 6;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 8);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ss = blockIdx.x, hv = blockIdx.y;
-    if (tid == 0) {
+    if (warp == kProdWarp && lane == 0) {
         tma_prefetch_desc(&maps.qpp);
         tma_prefetch_desc(&maps.oipp);
         tma_prefetch_desc(&maps.seghb);
     }
     pdl_wait();
     pdl_trigger();
-    if (ss == 0 && hv == 0 && blockIdx.z == 0) zero_unowned_tokens(p, tid, kThreads);
-    const SegSeq sq = warp_seg_seq(p, kBySeg, ss);
-    if (sq.n < 0 || ss >= p.SS) return;
-    int bos, eos;
-    seq_bounds(p.cu, p.cu64, sq.n, p.T, bos, eos);
-    const int seg_c0 = (ss - sq.sbase) * p.seg_m;  // first chunk of the segment (within the sequence)
-    const int c0 = seg_c0 + (int)blockIdx.z * kPair;
-    int nch = min(kPair, min(seg_c0 + p.seg_m, sq.nc) - c0);
-    nch = min(nch, p.S - (sq.cbase + c0));  // only a cu_seqlens that is not non-decreasing trims it
-    if (nch <= 0) return;
+    if (blockIdx.x == 0 && warp < kEpi / 32) zero_unowned_tokens(p, tid, kEpi);
+    const int npair = (p.seg_m + kPair - 1) / kPair;
+    const int total = p.SS * p.HV * npair;
     if (tid == 0) {
-        mbar_init(bar_l, 1);
-        mbar_init(bar_m, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(full + b, 1);
+            mbar_init(empty + b, kEpi / 32);
+            mbar_init(mfull + b, 1);
+            mbar_init(accfree + b, kEpi / 32);
+        }
         mbar_fence_init();
     }
-    if (warp == 0) tmem_alloc(tslot, 128);
+    if (warp == 0) tmem_alloc(tslot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    if (tid == 0) {
-        mbar_arrive_expect_tx(bar_l, 32768 + (uint32_t)nch * 32768u);
-        tma_load_3d(sm + kOffH, &maps.seghb, 0, ss * 128, hv, bar_l);
-        tma_load_3d(sm + kOffH + 16384, &maps.seghb, 64, ss * 128, hv, bar_l);
-        for (int i = 0; i < nch; ++i) {
-            const int row = (sq.cbase + c0 + i) * kChunk;
-            tma_load_3d(sm + kOffQ + 8192 * i, &maps.qpp, 0, row, hv, bar_l);
-            tma_load_3d(sm + kOffQ + 16384 + 8192 * i, &maps.qpp, 64, row, hv, bar_l);
-            tma_load_3d(sm + kOffO + 8192 * i, &maps.oipp, 0, row, hv, bar_l);
-            tma_load_3d(sm + kOffO + 16384 + 8192 * i, &maps.oipp, 64, row, hv, bar_l);
+    OutItem it;
+    if (warp == kProdWarp) {
+        int i = 0;
+        for (int w = blockIdx.x; w < total; w += gridDim.x) {
+            if (!seg_out_item(p, w, npair, it)) continue;
+            const int b = i & 1;
+            bool ok = true;
+            if (lane == 0) {
+                if (i >= 2) ok = mbar_wait(empty + b, (uint32_t)(((i >> 1) - 1) & 1), p.status, kErrScanTmaTimeout);
+                if (ok) {
+                    unsigned char* bf = sm + b * kBuf;
+                    mbar_arrive_expect_tx(full + b, 32768u + (uint32_t)it.nch * 32768u);
+                    tma_load_3d(bf + kOffH, &maps.seghb, 0, it.ss * 128, it.hv, full + b);
+                    tma_load_3d(bf + kOffH + 16384, &maps.seghb, 64, it.ss * 128, it.hv, full + b);
+                    for (int c = 0; c < it.nch; ++c) {
+                        const int row = (it.slot + c) * kChunk;
+                        tma_load_3d(bf + kOffQ + 8192 * c, &maps.qpp, 0, row, it.hv, full + b);
+                        tma_load_3d(bf + kOffQ + 16384 + 8192 * c, &maps.qpp, 64, row, it.hv, full + b);
+                        tma_load_3d(bf + kOffO + 8192 * c, &maps.oipp, 0, row, it.hv, full + b);
+                        tma_load_3d(bf + kOffO + 16384 + 8192 * c, &maps.oipp, 64, row, it.hv, full + b);
+                    }
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, (int)ok, 0)) break;
+            ++i;
         }
-    }
-    // thread (r, hf) = TMEM lane r (chunk c0 + r / 64, token row r % 64), columns 64 hf .. +63
-    const int r = lane + 32 * (warp & 3), hf = warp >> 2;
-    const int ci = r >> 6, m = r & 63;
-    const int slot = sq.cbase + c0 + ci;
-    const int t0 = bos + (c0 + ci) * kChunk;
-    const bool live = ci < nch && m < eos - t0;
-    // oi = Aqk u of the chunk (prep, column-group major [16][64][8] bf16), loaded while the MMA runs
-    uint4 oc[8];
-    if (live) {
-        const uint16_t* oi_row = p.oi + cg_off(hv, p.S, slot, 8 * hf) + m * 8;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) oc[g] = *reinterpret_cast<const uint4*>(oi_row + g * 512);
-    }
-    bool ok = mbar_wait(bar_l, 0, p.status, kErrScanTmaTimeout);
-    if (tid == 0 && ok) {
-        // [Q''_a; Q''_b] (128 x 128, K-major) x h_s (128 x 128, MN-major) -> TMEM columns 0-127
-        tc_fence_after();
+        // the last two items' copies have landed before the CTA can leave (bounded)
+        if (lane == 0)
+            for (int j = max(0, i - 2); j < i; ++j) mbar_wait(full + (j & 1), (uint32_t)((j >> 1) & 1), nullptr, 0);
+    } else if (warp == kMmaWarp) {
         constexpr uint32_t idesc = umma_idesc_bf16(128, 128, false, true);
+        int i = 0;
+        for (int w = blockIdx.x; w < total; w += gridDim.x) {
+            if (!seg_out_item(p, w, npair, it)) continue;
+            const int b = i & 1;
+            bool ok = true;
+            if (lane == 0) {
+                ok = mbar_wait(full + b, (uint32_t)((i >> 1) & 1), p.status, kErrScanTmaTimeout);
+                if (ok && i >= 2) ok = mbar_wait(accfree + b, (uint32_t)(((i >> 1) - 1) & 1), p.status, kErrScanMmaTimeout);
+                if (ok) {
+                    // [Q''_a; Q''_b] (128 x 128, K-major) x h_s (128 x 128, MN-major) -> accumulator b
+                    tc_fence_after();
+                    const uint32_t bf = sbase + (uint32_t)b * kBuf;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tmem, umma_desc_sw128(sbase + kOffQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
-                      umma_desc_sw128(sbase + kOffH + 2048u * kk, 16384, 1024), idesc, kk > 0);
-        umma_commit(bar_m);
-    }
-    ok = __syncthreads_and(ok);
-    if (ok) ok = mbar_wait(bar_m, 0, p.status, kErrScanMmaTimeout);
-    tc_fence_after();
-    if (ok) {
-        // o = scale (Q'' h_s + oi'' + oi) for this thread's 64 columns of its token row
-        uint16_t* dst = p.out + ((size_t)(t0 + m) * p.HV + hv) * kD + 64 * hf;
-        const unsigned char* orow = sm + kOffO + (uint32_t)hf * 16384u + (uint32_t)r * 128u;
-#pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-            uint32_t d[32];
-            tmem_ld32_async(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * hf + 32u * blk, d);
-            tmem_ld_wait();
-            tmem_regs_ready(d);
+                    for (int kk = 0; kk < 8; ++kk)
+                        umma_bf16(tmem + 128u * (uint32_t)b,
+                                  umma_desc_sw128(bf + kOffQ + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+                                  umma_desc_sw128(bf + kOffH + 2048u * kk, 16384, 1024), idesc, kk > 0);
+                    umma_commit(mfull + b);
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, (int)ok, 0)) break;
+            ++i;
+        }
+    } else {
+        // epilogue: thread (r, hf) = TMEM lane r (chunk r / 64 of the pair, token row r % 64), columns
+        // 64 hf .. +63: o = scale (Q'' h_s + oi'' + oi)
+        const int r = lane + 32 * (warp & 3), hf = warp >> 2;
+        const int ci = r >> 6, m = r & 63;
+        int i = 0;
+        for (int w = blockIdx.x; w < total; w += gridDim.x) {
+            if (!seg_out_item(p, w, npair, it)) continue;
+            const int b = i & 1;
+            const bool live = ci < it.nch && m < (ci ? it.L1 : it.L0);
+            const int slot = it.slot + ci;
+            // oi = Aqk u of the chunk (prep, column-group major [16][64][8] bf16), loaded first so its
+            // latency overlaps the wait for the product
+            uint4 oc[8];
             if (live) {
+                const uint16_t* oi_row = p.oi + cg_off(it.hv, p.S, slot, 8 * hf) + m * 8;
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const int g = 4 * blk + q4;
+                for (int g = 0; g < 8; ++g) oc[g] = *reinterpret_cast<const uint4*>(oi_row + g * 512);
+            }
+            const bool ok = mbar_wait(mfull + b, (uint32_t)((i >> 1) & 1), p.status, kErrScanMmaTimeout);
+            tc_fence_after();
+            if (!__all_sync(0xffffffffu, ok)) break;
+            uint32_t d[2][32];
+            tmem_ld32_async(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 128u * (uint32_t)b + 64u * hf, d[0]);
+            tmem_ld32_async(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 128u * (uint32_t)b + 64u * hf + 32u, d[1]);
+            tmem_ld_wait();
+            tmem_regs_ready(d[0]);
+            tmem_regs_ready(d[1]);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(accfree + b);  // accumulator b may take the next product
+            if (live) {
+                uint16_t* dst = p.out + ((size_t)(it.t0 + ci * kChunk + m) * p.HV + it.hv) * kD + 64 * hf;
+                const unsigned char* orow = sm + b * kBuf + kOffO + (uint32_t)hf * 16384u + (uint32_t)r * 128u;
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
                     const uint4 o2 = *reinterpret_cast<const uint4*>(orow + ((g ^ (r & 7)) << 4));
                     const uint32_t pw[4] = {o2.x, o2.y, o2.z, o2.w};
                     const uint32_t ow[4] = {oc[g].x, oc[g].y, oc[g].z, oc[g].w};
                     uint32_t pk[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float2 x2 = add2(add2(make_float2(__uint_as_float(d[8 * q4 + 2 * e]), __uint_as_float(d[8 * q4 + 2 * e + 1])),
+                        const uint32_t x0 = d[g >> 2][8 * (g & 3) + 2 * e], x1 = d[g >> 2][8 * (g & 3) + 2 * e + 1];
+                        const float2 x2 = add2(add2(make_float2(__uint_as_float(x0), __uint_as_float(x1)),
                                                     make_float2(__uint_as_float(pw[e] << 16), __uint_as_float(pw[e] & 0xffff0000u))),
                                                make_float2(__uint_as_float(ow[e] << 16), __uint_as_float(ow[e] & 0xffff0000u)));
                         pk[e] = pack_bf16x2(p.scale * x2.x, p.scale * x2.y);
@@ -669,13 +738,14 @@ __global__ void __launch_bounds__(sego::kThreads)
                     *reinterpret_cast<uint4*>(dst + 8 * g) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + b);  // buffer b (oi'') is read
+            ++i;
         }
-    } else if (tid == 0) {
-        mbar_wait(bar_l, 0, nullptr, 0);  // let copies in flight land (bounded) before the CTA exits
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 128);
+    if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream_t stream) {
@@ -694,10 +764,16 @@ int launch_prefill_seg(const PrefillArgs& p, const PrefillMaps& maps, cudaStream
     if (launch_pdl(gdn_prefill_seg_chain_kernel, dim3(kD / segc::BV, p.N, p.HV), dim3(segc::kThreads), segc::kSmem,
                    stream, p, maps) != cudaSuccess)
         return -1;
-    if (launch_pdl(gdn_prefill_seg_out_kernel,
-                   dim3((unsigned)std::max<long long>(segs, 1), p.HV, (p.seg_m + sego::kPair - 1) / sego::kPair),
-                   dim3(sego::kThreads), sego::kSmem, stream, p, maps) != cudaSuccess)
-        return -1;
+    {
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return -1;
+        const long long items = segs * p.HV * ((p.seg_m + sego::kPair - 1) / sego::kPair);
+        if (launch_pdl(gdn_prefill_seg_out_kernel, dim3((unsigned)std::max<long long>(1, std::min<long long>(items, sms))),
+                       dim3(sego::kThreads), sego::kSmem, stream, p, maps) != cudaSuccess)
+            return -1;
+    }
     return 0;
 }
 
