@@ -8,7 +8,9 @@ Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed
     Timed as CUDA-graph replays of K decode launches cycling over 8 state buffers
     (8 x 32 MiB = 256 MiB > the 126 MB L2, so every launch streams its state from HBM).
   * prefill_8k: one 8192-token sequence (cu_seqlens = [0, 8192], initial state N(0, 0.02)),
-    tokens/s; L2 flushed (256 MiB write) before every timed step, per-step CUDA events.
+    tokens/s; L2 flushed before every timed step (a 256 MiB write, then a 256 MiB read of another
+    buffer so that the write's dirty lines are written back outside the timed call), per-step
+    CUDA events.
   * decode_sweep (config 1): B = 1 .. 512, each over rotating state buffers (>= 384 MiB), beside
     the reference's published latencies.
   * prefill_configs: single sequences of 64 .. 4096 tokens (beside the reference's published table),
@@ -16,8 +18,9 @@ Workload per GPU (weak scaling: per-GPU work is fixed as N grows, ranks use seed
     and 8 packed 1024-token sequences per GPU, timed the same way; plus 64 x 4096 tokens split by
     sequence over the ranks (strong scaling; whole-job tokens/s over the slowest rank).
   * e2e: the same two metrics through the public API (gdn.decode.kernel / gdn.prefill.kernel)
-    with pinned host buffers: every step copies its inputs host->device and its results back,
-    pipelined over copy-in / compute / copy-out streams as a serving loop runs them.
+    with pinned host buffers: every step copies its inputs host->device and its results back
+    (one pinned host arena, one copy each way per step), pipelined over copy-in / compute /
+    copy-out streams as a serving loop runs them.
   * cpu_baseline: the CPU oracle (a C restatement of the reference's sequential PyTorch
     loops, all host threads) on a bounded sample of the same workload, rank 0 only.
 --impl reference times that same CPU oracle as the reference arm (the reference itself is
@@ -493,19 +496,29 @@ def main():
     pns = torch.empty((1, HV, D, D), dtype=torch.float32, device=dev)
     ws = torch.empty(gdn.prefill.workspace_bytes(1, T), dtype=torch.uint8, device=dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush_rd = torch.zeros(32 * 1024 * 1024, dtype=torch.int64, device=dev)
+
+    def flush_l2(clean=True):
+        # A 256 MiB write evicts everything earlier steps left in L2.  It leaves L2 full of its own
+        # dirty lines, whose write-back would then land inside the next timed call (~126 MB, about
+        # 20 us of HBM time at 8K); reading another 256 MiB afterwards writes them back here and
+        # leaves L2 holding clean, unrelated lines.  clean=False keeps the dirty-L2 variant.
+        flush.fill_(1)
+        if clean:
+            flush_rd.sum()
     from gdn import prefill as pmod
 
     def prefill_step(flags=0):
         pmod._launch(pq, pk, pv, ph0, A_log, pa, dt_bias, pb, cu, scale, pout, pns, workspace=ws, flags=flags)
 
-    def time_8k(flags):
+    def time_8k(flags, clean=True):
         for _ in range(args.warmup):
             prefill_step(flags)
         barrier()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.prefill_steps)]
         for e0, e1 in evs:
-            flush.fill_(1)
+            flush_l2(clean)
             torch.cuda._sleep(200_000)  # keeps the GPU busy while the host submits the call
             e0.record()
             prefill_step(flags)
@@ -514,7 +527,8 @@ def main():
         return max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs))
 
     pre_ms = time_8k(0)  # the library's default route (segmented for one 8192-token sequence)
-    pre_routes = {"segmented_ms": round(time_8k(0x10), 5), "single_pass_scan_ms": round(time_8k(0x8), 5)}
+    pre_routes = {"segmented_ms": round(time_8k(0x10), 5), "single_pass_scan_ms": round(time_8k(0x8), 5),
+                  "dirty_l2_flush_ms": round(time_8k(0, clean=False), 5)}
 
     # ---------------- other prefill configurations (reported alongside) ----------------
     def time_prefill(lens, with_state, steps=10):
@@ -536,7 +550,7 @@ def main():
         barrier()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         for e0, e1 in evs:
-            flush.fill_(1)
+            flush_l2()
             torch.cuda._sleep(200_000)  # keeps the GPU busy while the host submits the call
             e0.record()
             step()
@@ -611,14 +625,43 @@ def main():
 
     # ---------------- e2e through the public API with pinned host buffers ----------------
     # Every step copies its inputs host -> device from pinned memory, runs the public call and
-    # copies its results back; steps are pipelined as a serving loop would run them: copy-in,
-    # compute and copy-out on three streams over a ring of three device buffer sets, so step i's
-    # device -> host copy overlaps step i + 1's host -> device copy (PCIe is full duplex).  The
-    # timed region runs from the first copy-in to the last copy-out.
-    def pipelined_e2e(h_in, launch, n_steps, n_bufs=3):
+    # copies its results back.  A serving loop stages a step's tensors in one pinned host arena
+    # and one device arena per buffer set (the tensors are views into it), so each step is one
+    # host -> device copy of [inputs | state] and one device -> host copy of [state or outputs]:
+    # six separate copies per step measured ~6% slower on the same box (per-copy setup, and
+    # small copies interleaved with the large ones in each direction).  Steps are pipelined:
+    # copy-in, compute and copy-out on three streams over a ring of three device arenas, so
+    # step i's device -> host copy overlaps step i + 1's host -> device copy (PCIe is full
+    # duplex).  The timed region runs from the first copy-in to the last copy-out.
+    def arena_layout(specs):
+        """specs: (shape, dtype) list -> (byte offsets 256-aligned, total bytes)."""
+        offs, off = [], 0
+        for shape, dt in specs:
+            offs.append(off)
+            nbytes = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+            off = (off + nbytes + 255) // 256 * 256
+        return offs, off
+
+    def arena_views(buf, specs, offs):
+        return [buf[o:o + math.prod(sh) * torch.empty((), dtype=dt).element_size()].view(dt).view(sh)
+                for (sh, dt), o in zip(specs, offs)]
+
+    def pipelined_e2e(h_in, out_specs, launch, n_steps, inout_last=False, n_bufs=3):
+        """h_in: host tensors copied in every step; out_specs: (shape, dtype) of the results copied
+        back.  With inout_last the last input is updated in place and copied back too (decode's
+        state).  launch(ins, outs) makes the public call on device views."""
+        specs = [(tuple(t.shape), t.dtype) for t in h_in] + list(out_specs)
+        offs, total = arena_layout(specs)
+        n_in = len(h_in)
+        h2d_end = offs[n_in - 1] + h_in[-1].numel() * h_in[-1].element_size()
+        d2h_begin = offs[n_in - 1] if inout_last else offs[n_in]
+        h_arena = torch.empty(total, dtype=torch.uint8).pin_memory()
+        for t, v_ in zip(h_in, arena_views(h_arena, specs, offs)):
+            v_.copy_(t)
+        d_arena = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(n_bufs)]
+        d_views = [arena_views(d, specs, offs) for d in d_arena]
+        h_back = [torch.empty(total - d2h_begin, dtype=torch.uint8).pin_memory() for _ in range(n_bufs)]
         s_in, s_run, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
-        d_in = [[torch.empty_like(t, device=dev) for t in h_in] for _ in range(n_bufs)]
-        h_out = [None] * n_bufs
         ev_in = [torch.cuda.Event() for _ in range(n_bufs)]
         ev_run = [torch.cuda.Event() for _ in range(n_bufs)]
         ev_out = [torch.cuda.Event() for _ in range(n_bufs)]
@@ -629,19 +672,15 @@ def main():
                 if i >= n_bufs:
                     s_in.wait_event(ev_out[j])  # buffer set j is free again
                 with torch.cuda.stream(s_in):
-                    for d, h in zip(d_in[j], h_in):
-                        d.copy_(h, non_blocking=True)
+                    d_arena[j][:h2d_end].copy_(h_arena[:h2d_end], non_blocking=True)
                     ev_in[j].record(s_in)
                 s_run.wait_event(ev_in[j])
                 with torch.cuda.stream(s_run):
-                    outs = launch(j, d_in[j])
+                    launch(d_views[j][:n_in], d_views[j][n_in:])
                     ev_run[j].record(s_run)
-                if h_out[j] is None:
-                    h_out[j] = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
                 s_out.wait_event(ev_run[j])
                 with torch.cuda.stream(s_out):
-                    for h, d in zip(h_out[j], outs):
-                        h.copy_(d, non_blocking=True)
+                    h_back[j].copy_(d_arena[j][d2h_begin:], non_blocking=True)
                     ev_out[j].record(s_out)
 
         cur = torch.cuda.current_stream(dev)
@@ -657,7 +696,7 @@ def main():
         t1.record(s_out)
         torch.cuda.synchronize()
         barrier()
-        return max_over_ranks(t0.elapsed_time(t1) / n_steps)
+        return max_over_ranks(t0.elapsed_time(t1) / n_steps), h2d_end, total - d2h_begin
 
     def host_link_rates(nbytes=64 << 20, reps=5):
         """H2D and D2H copy rates of this rank from pinned memory, all ranks copying at the same
@@ -687,35 +726,27 @@ def main():
             dist.all_gather_object(allr, {**link, **host_binding})
             link = {"per_rank": allr}
         n_e2e = max(6, min(30, args.steps // 8))
-        h_dec = [t.cpu().pin_memory() for t in (q, k, v, a, b, states[0])]
-        dec_out = [torch.empty_like(out) for _ in range(3)]
+        h_dec = [t.cpu() for t in (q, k, v, a, b, states[0])]
 
-        def dec_launch(j, d):  # in place: the state buffer is also new_state
-            gdn.decode.kernel(d[0], d[1], d[2], d[5], A_log, d[3], dt_bias, d[4], scale, dec_out[j], d[5])
-            return [dec_out[j], d[5]]
+        def dec_launch(d, o):  # in place: the state view is also new_state
+            gdn.decode.kernel(d[0], d[1], d[2], d[5], A_log, d[3], dt_bias, d[4], scale, o[0], d[5])
 
-        h2d = sum(t.numel() * t.element_size() for t in h_dec)
-        d2h = out.numel() * out.element_size() + states[0].numel() * 4
-        e2e_ms = pipelined_e2e(h_dec, dec_launch, n_e2e)
+        e2e_ms, h2d, d2h = pipelined_e2e(h_dec, [(tuple(out.shape), out.dtype)], dec_launch, n_e2e, inout_last=True)
         e2e = {"value": round(world * DECODE_STATE_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "pipeline": "copy-in / compute / copy-out streams, 3 buffer sets, pinned host memory"}
+               "pipeline": "copy-in / compute / copy-out streams, 3 device arenas, one pinned host arena: one H2D and one D2H copy per step"}
 
         hcu = torch.tensor([0, T], dtype=torch.int32)
-        h_pre = [t.cpu().pin_memory() for t in (pq, pk, pv, pa, pb, ph0)] + [hcu.pin_memory()]
-        pre_out = [(torch.empty_like(pout), torch.empty_like(pns)) for _ in range(3)]
+        h_pre = [t.cpu() for t in (pq, pk, pv, pa, pb, hcu, ph0)]
 
-        def pre_launch(j, d):
-            o, s_ = pre_out[j]
-            gdn.prefill.kernel(d[0], d[1], d[2], d[5], A_log, d[3], dt_bias, d[4], d[6], scale, o, s_)
-            return [o, s_]
+        def pre_launch(d, o):
+            gdn.prefill.kernel(d[0], d[1], d[2], d[6], A_log, d[3], dt_bias, d[4], d[5], scale, o[0], o[1])
 
-        ph2d = sum(t.numel() * t.element_size() for t in h_pre)
-        pd2h = pout.numel() * 2 + pns.numel() * 4
-        pe_ms = pipelined_e2e(h_pre, pre_launch, n_e2e)
+        pe_ms, ph2d, pd2h = pipelined_e2e(h_pre, [(tuple(pout.shape), pout.dtype), (tuple(pns.shape), pns.dtype)],
+                                          pre_launch, n_e2e)
         pre_e2e = {"value": round(world * T / (pe_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(pe_ms, 4),
                    "h2d_bytes_per_step": ph2d, "d2h_bytes_per_step": pd2h,
-                   "pipeline": "copy-in / compute / copy-out streams, 3 buffer sets, pinned host memory"}
+                   "pipeline": "copy-in / compute / copy-out streams, 3 device arenas, one pinned host arena: one H2D and one D2H copy per step"}
 
     # ---------------- report ----------------
     if rank != 0:
@@ -764,7 +795,7 @@ def main():
                      "kernel": "gdn_decode_kernel", "peak_source": peak_src},
         "prefill_8k": {
             "tokens_per_s": round(world * T / (pre_ms * 1e-3), 1), "ms_per_step": round(pre_ms, 5),
-            "config": "one 8192-token sequence per GPU, cu_seqlens int32, initial state N(0,0.02); L2 flushed",
+            "config": "one 8192-token sequence per GPU, cu_seqlens int32, initial state N(0,0.02); L2 flushed (256 MiB write, then a 256 MiB read of another buffer) before each call",
             "roofline": {"bound": "max(hbm, tensor)", "achieved_frac": round(pre_bound_s / (pre_ms * 1e-3), 5),
                          "bound_us": round(pre_bound_s * 1e6, 3), "alg_bytes": pre_bytes, "alg_flops": pre_flops,
                          "traffic": NCU_TRAFFIC["prefill_8k_call"], "traffic_scope": "all kernels of one call",

@@ -521,11 +521,16 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     const int c = 4 * ch_half + cc;
+                    // two 16-byte reads per 8 columns: rows are 272 bytes apart, so the eight threads of
+                    // each 128-byte phase hit disjoint bank groups (scalar reads conflicted four ways)
+                    const float4 ta = *reinterpret_cast<const float4*>(Trow + 8 * c);
+                    const float4 tb = *reinterpret_cast<const float4*>(Trow + 8 * c + 4);
+                    const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
                     uint32_t pk[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int j = 8 * c + 2 * e;
-                        float t0 = Trow[j], t1 = Trow[j + 1];
+                        float t0 = tv[2 * e], t1 = tv[2 * e + 1];
                         if (ub) {
                             t0 = (j == m ? t0 - 1.f : t0) * Bs[j];
                             t1 = (j + 1 == m ? t1 - 1.f : t1) * Bs[j + 1];
