@@ -527,6 +527,44 @@ def main():
         return max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs))
 
     pre_ms = time_8k(0)  # the library's default route (segmented for one 8192-token sequence)
+
+    # the same sequence split by v-head over the ranks (gdn.shard.head_shard: each rank runs its q/k
+    # head group, no exchange), strong scaling; at N = 1 also the pieces a 4- and an 8-GPU split run
+    from gdn.shard import head_shard
+
+    def time_8k_heads(world_, rank_):
+        h0, h1, v0, v1 = head_shard(H, HV, world_, rank_, prefill=True)
+        xq, xk = pq[:, h0:h1].contiguous(), pk[:, h0:h1].contiguous()
+        xv, xa, xb = pv[:, v0:v1].contiguous(), pa[:, v0:v1].contiguous(), pb[:, v0:v1].contiguous()
+        xh, xA, xdt = ph0[:, v0:v1].contiguous(), A_log[v0:v1].contiguous(), dt_bias[v0:v1].contiguous()
+        xo = torch.empty((T, v1 - v0, D), dtype=torch.bfloat16, device=dev)
+        xs = torch.empty((1, v1 - v0, D, D), dtype=torch.float32, device=dev)
+        xws = torch.empty(gdn.prefill.workspace_bytes(1, T, num_qk_heads=h1 - h0, num_v_heads=v1 - v0), dtype=torch.uint8, device=dev)
+
+        def step():
+            pmod._launch(xq, xk, xv, xh, xA, xa, xdt, xb, cu, scale, xo, xs, workspace=xws)
+
+        for _ in range(args.warmup):
+            step()
+        barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.prefill_steps)]
+        for e0, e1 in evs:
+            flush_l2()
+            torch.cuda._sleep(200_000)
+            e0.record()
+            step()
+            e1.record()
+        barrier()
+        return max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)), (h1 - h0, v1 - v0)
+
+    hs_ms, hs_heads = time_8k_heads(world, rank)
+    head_split = {"ms_per_step": round(hs_ms, 5), "tokens_per_s": round(T / (hs_ms * 1e-3), 1),
+                  "heads_per_rank": {"qk": hs_heads[0], "v": hs_heads[1]},
+                  "scaling": "strong: one 8192-token sequence split by v-head over the ranks (gdn.shard.head_shard)"}
+    if world == 1:
+        head_split["one_rank_of_4_ms"] = round(time_8k_heads(4, 0)[0], 5)
+        head_split["one_rank_of_8_ms"] = round(time_8k_heads(8, 0)[0], 5)
     pre_routes = {"segmented_ms": round(time_8k(0x10), 5), "single_pass_scan_ms": round(time_8k(0x8), 5),
                   "dirty_l2_flush_ms": round(time_8k(0, clean=False), 5)}
 
@@ -801,6 +839,7 @@ def main():
                          "traffic": NCU_TRAFFIC["prefill_8k_call"], "traffic_scope": "all kernels of one call",
                          "peak_source": peak_src},
             "routes": pre_routes,
+            "head_split": head_split,
             "e2e": pre_e2e,
         },
         "prefill_configs": prefill_more,

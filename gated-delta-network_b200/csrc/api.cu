@@ -49,13 +49,12 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Head size 128; any number of q/k heads H with HV a multiple of H (grouped v-heads).  The
 // reference asserts H = 4, HV = 8 (reference/gdn_decode_ref.py:32-36); other counts are a
-// superset (e.g. the qk16_v32 family).  Prefill also needs HV a multiple of 8 (its gate
-// tiles are TMA boxes of 8 heads).
+// superset (e.g. the qk16_v32 family, or one q/k head group of the reference's heads per GPU).
 bool shape_ok(int H, int HV, int K, int V) {
     return H >= 1 && H <= GDN_MAX_QK_HEADS && HV >= H && HV <= GDN_MAX_V_HEADS && HV % H == 0 && K == GDN_HEAD_DIM &&
            V == GDN_HEAD_DIM;
 }
-bool prefill_shape_ok(int H, int HV, int K, int V) { return shape_ok(H, HV, K, V) && HV % 8 == 0; }
+bool prefill_shape_ok(int H, int HV, int K, int V) { return shape_ok(H, HV, K, V); }
 
 int decode_variant(int B, int HV, unsigned flags) {
     const unsigned forced = (flags >> 8) & 0xffu;  // tuning override: variant + 1
@@ -117,8 +116,10 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* st
     if (N == 0) return GDN_OK;
     if (!cu_seqlens || !new_state || !A_log || !dt_bias) return GDN_ERR_NULL;
     if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL;
-    if ((T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(a) || !aligned16(b) ||
-                   !aligned16(out))) ||
+    // the gates are TMA tiles when HV is a multiple of 8 (16-byte rows), plain bf16 loads otherwise
+    const bool gates_ok = HV % 8 == 0 ? aligned16(a) && aligned16(b)
+                                      : (reinterpret_cast<uintptr_t>(a) & 1u) == 0 && (reinterpret_cast<uintptr_t>(b) & 1u) == 0;
+    if ((T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !gates_ok || !aligned16(out))) ||
         !aligned16(new_state) ||
         (state && !aligned16(state)))
         return GDN_ERR_ALIGN;
@@ -191,7 +192,7 @@ const char* gdn_status_string(int status) {
     switch (status) {
         case GDN_OK: return "ok";
         case GDN_ERR_NULL: return "a required pointer is NULL";
-        case GDN_ERR_SHAPE: return "unsupported shape (need K=V=128, HV a multiple of H; prefill: HV a multiple of 8)";
+        case GDN_ERR_SHAPE: return "unsupported shape (need K=V=128, HV a multiple of H)";
         case GDN_ERR_ALIGN: return "a tensor pointer is not 16-byte aligned";
         case GDN_ERR_SIZE: return "invalid size or option";
         case GDN_ERR_WORKSPACE: return "workspace missing, misaligned (256 B) or too small";

@@ -36,7 +36,9 @@ struct PrefillArgs {
     const void* cu;        // [N+1] int32 / int64
     int cu64;
     int N, T;
-    int H, HV;             // q/k heads and v heads (HV a multiple of H and of 8; 4 and 8 in the reference)
+    int H, HV;             // q/k heads and v heads (HV a multiple of H; 4 and 8 in the reference)
+    int gates_tma;         // 1: HV a multiple of 8, the prep loads the gates as [64 tokens][8 heads] TMA
+                           //    boxes; 0: a gate row is under 16 bytes or not a whole box, plain loads
     int S;                 // chunk slots in the workspace (>= number of 64-token chunks)
     int test_withhold;     // GDN_FLAG_TEST_WITHHOLD_CHUNK: the scan skips chunk 1's copies
     int short_path;        // 1: sequences of 0..kShortLen tokens go to a short-sequence kernel, and
@@ -94,11 +96,16 @@ __host__ __device__ constexpr size_t prefill_up256(size_t x) { return (x + 255) 
 // the call.  Few sequences of many chunks: the chain of one sequence is the critical path, and
 // splitting it into segments whose transitions are built in parallel shortens it.  The segment
 // length is the shortest that keeps the local-transition grid (two CTAs per segment and v-head)
-// within one wave of 148 SMs.
+// within one wave of 148 SMs, but not so short that the chain over segments outgrows the local
+// chains: a local chunk step costs about three chain steps (B200: ~5.4 K vs ~1.8 K cycles), so
+// m^2 >= chunks / 3 per sequence.  The second bound only binds with few v-heads per call (a
+// sequence split over GPUs by v-head); with 8 v-heads the one-wave bound is the larger.
 __host__ __device__ constexpr int prefill_seg_m(int N, int T, int HV) {
     if (N < 1 || N > 32 || HV < 1 || T < 512 * N) return 0;  // N <= kSmallN; >= 8 chunks per sequence on average
     const long long nc = ((long long)T + 63) / 64;
-    for (int m = 2; m <= 64; ++m) {
+    int m_bal = 2;
+    while (3LL * m_bal * m_bal < nc / N) ++m_bal;
+    for (int m = m_bal; m <= 64; ++m) {
         const long long segs = (nc + m - 1) / m + (N - 1);  // bound on sum_n ceil(nc_n / m)
         if (segs * 2 * HV <= 148) return m;
     }

@@ -145,8 +145,12 @@ bool build_prefill_maps(const PrefillArgs& p, PrefillMaps* m) {
     ok = ok && map3d(&m->k, p.k, BF, 128, H, T, 256, 256 * H, 64, 1, 64, SW);
     ok = ok && map3d(&m->v, p.v, BF, 128, HV, T, 256, 256 * HV, 64, 1, 64, SW);
     // Gates: [T][HV] bf16 as (head, token); one box = 8 heads (the group of v-head hv) of 64 tokens (1 KB).
-    ok = ok && map2d(&m->a, p.a, BF, HV, T, 2 * HV, 8, 64);
-    ok = ok && map2d(&m->b, p.b, BF, HV, T, 2 * HV, 8, 64);
+    // A tensor map needs 16-byte row strides, so with HV not a multiple of 8 the prep reads the
+    // gates with plain loads and no map is built.
+    if (p.gates_tma) {
+        ok = ok && map2d(&m->a, p.a, BF, HV, T, 2 * HV, 8, 64);
+        ok = ok && map2d(&m->b, p.b, BF, HV, T, 2 * HV, 8, 64);
+    }
     // Workspace: [8][R][cols] as (col, row, head); one box = one 64-row chunk slot.
     ok = ok && map3d(&m->w, p.w, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
     ok = ok && map3d(&m->qp, p.qp, BF, 128, R, HV, 256, R * 256, 64, 64, 1, SW);
@@ -168,6 +172,7 @@ static int launch_scan(const PrefillArgs& p, const PrefillMaps& maps, int bv, cu
 int launch_prefill(const PrefillArgs& args, int bv, cudaStream_t stream) {
     if (args.N <= 0) return 0;
     PrefillArgs p = args;
+    p.gates_tma = p.HV % 8 == 0 ? 1 : 0;
     // Short sequences (0..kShortLen tokens) take a dedicated one-launch kernel in batches of many
     // sequences, where its throughput wins; with few sequences the chunked kernels process the
     // short ones off the critical path of the longest sequence, and a separate launch would only

@@ -138,8 +138,10 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
         tma_prefetch_desc(&maps.q);
         tma_prefetch_desc(&maps.k);
         tma_prefetch_desc(&maps.v);
-        tma_prefetch_desc(&maps.a);
-        tma_prefetch_desc(&maps.b);
+        if (p.gates_tma) {
+            tma_prefetch_desc(&maps.a);
+            tma_prefetch_desc(&maps.b);
+        }
     }
     pdl_wait();  // inputs and the chunk table come from earlier work on the stream
     // Without a chunk-table kernel this is the call's first kernel: reset the status word here,
@@ -214,9 +216,11 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                     mbar_init(bar_gate, 1);
                     mbar_fence_init();
                 }
-                mbar_arrive_expect_tx(bar_gate, 2 * 1024);
-                tma_load_2d(misc + kOffTileA, &maps.a, hv & ~7, bos, bar_gate);
-                tma_load_2d(misc + kOffTileB, &maps.b, hv & ~7, bos, bar_gate);
+                if (p.gates_tma) {
+                    mbar_arrive_expect_tx(bar_gate, 2 * 1024);
+                    tma_load_2d(misc + kOffTileA, &maps.a, hv & ~7, bos, bar_gate);
+                    tma_load_2d(misc + kOffTileB, &maps.b, hv & ~7, bos, bar_gate);
+                }
                 mbar_arrive_expect_tx(bar_load, 6 * 8192);
                 tma_load_3d(sm + kOffK0, &maps.k, 0, hq, bos, bar_load);
                 tma_load_3d(sm + kOffK1, &maps.k, 64, hq, bos, bar_load);
@@ -250,13 +254,19 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
             if (warp == 2 || warp == 3) {
                 // g, beta of token t from the a / b tiles ([64 tokens][8 heads] bf16); padded tokens
                 // (t >= L) carry g = 0, so their cumulative G repeats G_{L-1}, and beta = 0.
-                ok = mbar_wait(bar_gate, ph, p.status, kErrPrepTmaTimeout);
                 const int t = tid - 64;
                 float gl = 0.f, be = 0.f;
-                if (ok && t < L) {
-                    gl = log_decay(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileA)[t * 8 + (hv & 7)]), p.A_log[hv],
-                                   p.dt_bias[hv]);
-                    be = sigmoidf_(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileB)[t * 8 + (hv & 7)]));
+                if (p.gates_tma) {
+                    ok = mbar_wait(bar_gate, ph, p.status, kErrPrepTmaTimeout);
+                    if (ok && t < L) {
+                        gl = log_decay(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileA)[t * 8 + (hv & 7)]),
+                                       p.A_log[hv], p.dt_bias[hv]);
+                        be = sigmoidf_(bf2f(reinterpret_cast<const uint16_t*>(misc + kOffTileB)[t * 8 + (hv & 7)]));
+                    }
+                } else if (t < L) {  // [T][HV] rows narrower than a TMA box: one element per token
+                    const size_t gi = (size_t)(bos + t) * p.HV + hv;
+                    gl = log_decay(bf2f(p.a[gi]), p.A_log[hv], p.dt_bias[hv]);
+                    be = sigmoidf_(bf2f(p.b[gi]));
                 }
                 float x = gl;
 #pragma unroll
@@ -307,7 +317,7 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
             if (tid == 0) {
                 // MMA #1: [K; Q] (128 x 128) x K^T -> TMEM columns 0..63 (issued only if every tile
                 // landed, so a CTA that gives up never leaves an MMA in flight)
-                ok = mbar_wait(bar_gate, ph, p.status, kErrPrepTmaTimeout) &&
+                ok = (!p.gates_tma || mbar_wait(bar_gate, ph, p.status, kErrPrepTmaTimeout)) &&
                      mbar_wait(bar_load, ph, p.status, kErrPrepTmaTimeout);
                 if (ok) {
                     tc_fence_after();

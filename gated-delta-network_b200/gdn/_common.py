@@ -24,16 +24,14 @@ def resolve_scale(scale) -> float:
 def check_heads(Hq: int, Hk: int, HV: int, K: int, V: int, prefill: bool = False) -> None:
     """The reference asserts 4 q/k heads, 8 v-heads and head size 128
     (reference/gdn_decode_ref.py:32-36, reference/gdn_prefill_ref.py:33-36).  This library
-    accepts any head counts with HV a multiple of H (v-head hv reads q/k head hv // (HV // H)),
-    and for prefill HV a multiple of 8; the head size stays 128."""
+    accepts any head counts with HV a multiple of H (v-head hv reads q/k head hv // (HV // H));
+    the head size stays 128."""
     if Hk != Hq:
         raise ValueError(f"q and k must have the same number of heads (got {Hq} and {Hk})")
     if K != HEAD_DIM or V != HEAD_DIM:
         raise ValueError(f"head size must be {HEAD_DIM} (got K={K}, V={V})")
     if not (1 <= Hq <= HV and HV % Hq == 0):
         raise ValueError(f"v-heads must be a multiple of the q/k heads (got H={Hq}, HV={HV})")
-    if prefill and HV % 8:
-        raise ValueError(f"prefill needs a multiple of 8 v-heads (got HV={HV})")
 
 
 def cuda_device(t: torch.Tensor, name: str) -> torch.device:

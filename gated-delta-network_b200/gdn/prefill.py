@@ -31,7 +31,7 @@ def _launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     HV, V = v.shape[1], v.shape[2]
     N = cu_seqlens.shape[0] - 1
     # Shape contract of the reference oracle (reference/gdn_prefill_ref.py:33-36), widened to any
-    # head counts with HV a multiple of H and of 8.
+    # head counts with HV a multiple of H.
     check_heads(Hq, Hk, HV, K, V, prefill=True)
     if N < 0:
         raise ValueError("cu_seqlens must hold at least one element")
@@ -88,7 +88,7 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
 
     q, k [T,4,128] bf16; v [T,8,128] bf16; state [N,8,128,128] fp32 or None; a, b [T,8] bf16;
     cu_seqlens [N+1] int32/int64; scale float, 0-d tensor, or None/0 (1/sqrt(128)).
-    Head counts: the reference's 4 q/k heads and 8 v-heads, or any H, HV with HV a multiple of H and of 8
+    Head counts: the reference's 4 q/k heads and 8 v-heads, or any H, HV with HV a multiple of H
     (v-head hv reads q/k head hv // (HV // H)); the shapes above then read H for 4 and HV for 8.
     Tokens outside every sequence keep a zero output, and a zero-length sequence
     gets an all-zero final state, as in the reference oracle.

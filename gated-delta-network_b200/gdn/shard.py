@@ -47,26 +47,35 @@ def seq_shard(cu_seqlens: Sequence[int], world: int, rank: int):
 
 def head_shard(num_qk_heads: int, num_v_heads: int, world: int, rank: int, prefill: bool = False):
     """Split the heads of a call over ranks, for calls with fewer independent sequences (or batch
-    elements) than ranks.  Each q/k head and the v-heads that read it (v-head hv reads q/k head
-    hv // (HV // H)) stay on one rank, so the shards exchange nothing.
+    elements) than ranks.  Each rank takes HV / world consecutive v-heads and the q/k heads they
+    read (v-head hv reads q/k head hv // (HV // H)); v-heads never exchange anything, so neither do
+    the shards.  A rank holds whole q/k head groups, or part of one group (then it reads one q/k
+    head that another rank reads too: an input, copied, not exchanged).
 
-    Returns (qk_start, qk_stop, v_start, v_stop): the rank's q/k heads and v-heads.  The rank
-    runs the path on q[..., qk_start:qk_stop, :], k likewise, and v, a, b, A_log, dt_bias and the
-    state sliced to [v_start, v_stop) along their head dimension.
+    Returns (qk_start, qk_stop, v_start, v_stop).  The rank runs the path on
+    q[..., qk_start:qk_stop, :], k likewise, and v, a, b, A_log, dt_bias and the state sliced to
+    [v_start, v_stop) along their head dimension; its local call then has HV / world v-heads
+    reading qk_stop - qk_start q/k heads in the same grouped order.
 
-    The split needs world to divide the number of q/k heads.  Prefill kernels read the gates in
-    8-head tiles, so with prefill=True each rank must also keep a multiple of 8 v-heads (e.g. the
-    32-v-head family over up to 4 ranks); a split that cannot satisfy these raises ValueError.
+    world must divide HV, and each rank's v-heads must be whole groups or an equal part of one
+    group; otherwise ValueError.  The reference's 4 q/k heads and 8 v-heads split over 2, 4 or 8
+    ranks (8: one v-head and its q/k head per rank), so one long sequence can use every GPU of a
+    box.  Decode and prefill take the same splits (prefill is accepted and changes nothing).
     """
     H, HV = int(num_qk_heads), int(num_v_heads)
     if world <= 0 or not 0 <= rank < world:
         raise ValueError("need world > 0 and 0 <= rank < world")
     if H <= 0 or HV % H:
         raise ValueError(f"v-heads ({HV}) must be a multiple of q/k heads ({H})")
-    if H % world:
-        raise ValueError(f"{world} ranks cannot split {H} q/k heads into equal groups")
-    hq = H // world
+    if HV % world:
+        raise ValueError(f"{world} ranks cannot split {HV} v-heads into equal groups")
+    group = HV // H  # v-heads per q/k head
     hv = HV // world
-    if prefill and hv % 8:
-        raise ValueError(f"prefill needs a multiple of 8 v-heads per rank (got {hv})")
-    return rank * hq, (rank + 1) * hq, rank * hv, (rank + 1) * hv
+    v0, v1 = rank * hv, (rank + 1) * hv
+    if hv >= group:
+        if hv % group:
+            raise ValueError(f"{hv} v-heads per rank would split a group of {group}")
+        return v0 // group, v1 // group, v0, v1
+    if group % hv:
+        raise ValueError(f"{hv} v-heads per rank do not divide a group of {group}")
+    return v0 // group, v0 // group + 1, v0, v1

@@ -82,9 +82,9 @@ enum gdn_status {
 #define GDN_NUM_V_HEADS 8
 #define GDN_HEAD_DIM 128
 /* Other head counts are accepted as a superset of the reference: H q/k heads, HV v-heads with
- * HV a multiple of H (v-head hv reads q/k head hv / (HV / H)), 1 <= H <= 64, HV <= 256; prefill
- * also needs HV a multiple of 8.  Head size stays 128.  Layouts generalise the ones below with
- * 4 -> H and 8 -> HV. */
+ * HV a multiple of H (v-head hv reads q/k head hv / (HV / H)), 1 <= H <= 64, HV <= 256, for decode
+ * and prefill alike (so one q/k head group of the reference's heads, e.g. H = 1, HV = 2, runs on
+ * its own GPU).  Head size stays 128.  Layouts generalise the ones below with 4 -> H and 8 -> HV. */
 #define GDN_MAX_QK_HEADS 64
 #define GDN_MAX_V_HEADS 256
 #define GDN_CHUNK 64

@@ -34,17 +34,25 @@ def test_seq_shard_rebases_and_covers():
 
 
 def test_head_shard_groups_and_constraints():
-    # decode, the reference family (4 q/k heads, 8 v-heads): 1, 2 or 4 ranks
-    for world in (1, 2, 4):
-        parts = [head_shard(4, 8, world, r) for r in range(world)]
-        assert parts[0][0] == 0 and parts[-1][1] == 4 and parts[0][2] == 0 and parts[-1][3] == 8
-        for a0, a1, b0, b1 in parts:
-            assert b0 == a0 * 2 and b1 == a1 * 2  # each v-head stays with the q/k head it reads
-    with pytest.raises(ValueError):
-        head_shard(4, 8, 3, 0)  # 3 does not divide 4 q/k heads
-    with pytest.raises(ValueError):
-        head_shard(4, 8, 2, 0, prefill=True)  # 4 v-heads per rank: below the 8-head gate tiles
+    # the reference family (4 q/k heads, 8 v-heads): 1, 2, 4 or 8 ranks, decode and prefill alike
+    for world in (1, 2, 4, 8):
+        for prefill in (False, True):
+            parts = [head_shard(4, 8, world, r, prefill=prefill) for r in range(world)]
+            assert parts[0][2] == 0 and parts[-1][3] == 8
+            assert all(parts[i][3] == parts[i + 1][2] for i in range(world - 1))  # v-heads tile [0, 8)
+            for a0, a1, b0, b1 in parts:
+                # every v-head of the rank reads one of the rank's q/k heads, in grouped order
+                assert all(a0 <= hv // 2 < a1 for hv in range(b0, b1))
+                assert (b1 - b0) % (a1 - a0) == 0
+    assert head_shard(4, 8, 8, 5) == (2, 3, 5, 6)  # v-head 5 reads q/k head 2
+    assert head_shard(4, 8, 2, 1, prefill=True) == (2, 4, 4, 8)
     assert head_shard(16, 32, 4, 3, prefill=True) == (12, 16, 24, 32)
+    with pytest.raises(ValueError):
+        head_shard(4, 8, 3, 0)  # 3 does not divide 8 v-heads
+    with pytest.raises(ValueError):
+        head_shard(3, 6, 2, 0)  # 3 v-heads per rank: one and a half groups of 2
+    with pytest.raises(ValueError):
+        head_shard(2, 12, 3, 0)  # 4 v-heads per rank do not divide a group of 6
 
 
 def _free_port():
@@ -91,8 +99,14 @@ def _worker(rank, world, port, q):
         hpo = oracle.prefill(hp["q"][:, h0:h1], hp["k"][:, h0:h1], hp["v"][:, v0:v1], hp["state"][:, v0:v1],
                              hp["A_log"][v0:v1], hp["a"][:, v0:v1], hp["dt_bias"][v0:v1], hp["b"][:, v0:v1],
                              hp["cu_seqlens"], hp["scale"], threads=1)
+        # prefill of the reference family (4 q/k heads, 8 v-heads) split by v-heads
+        rp = gi.prefill_inputs([130], seed=7)
+        h0, h1, v0, v1 = head_shard(4, 8, world, rank, prefill=True)
+        rpo = oracle.prefill(rp["q"][:, h0:h1], rp["k"][:, h0:h1], rp["v"][:, v0:v1], rp["state"][:, v0:v1],
+                             rp["A_log"][v0:v1], rp["a"][:, v0:v1], rp["dt_bias"][v0:v1], rp["b"][:, v0:v1],
+                             rp["cu_seqlens"], rp["scale"], threads=1)
         heads = [None] * world
-        dist.all_gather_object(heads, (ho, hpo))
+        dist.all_gather_object(heads, (ho, hpo, rpo))
         t = torch.tensor([float(rank + 1)], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         if rank == 0:
@@ -138,3 +152,8 @@ def test_two_rank_sharded_oracle_matches_single_process():
                             hp["cu_seqlens"], hp["scale"])
     assert np.array_equal(np.concatenate([x[1][0] for x in heads], axis=1), po)
     assert np.array_equal(np.concatenate([x[1][1] for x in heads], axis=1), ps)
+    rp = gi.prefill_inputs([130], seed=7)
+    po, ps = oracle.prefill(rp["q"], rp["k"], rp["v"], rp["state"], rp["A_log"], rp["a"], rp["dt_bias"], rp["b"],
+                            rp["cu_seqlens"], rp["scale"])
+    assert np.array_equal(np.concatenate([x[2][0] for x in heads], axis=1), po)
+    assert np.array_equal(np.concatenate([x[2][1] for x in heads], axis=1), ps)
