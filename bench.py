@@ -60,9 +60,9 @@ REPS = 5  # timed repetitions of every measurement; the median is reported
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum), or None.
 # Source: the ncu summaries under profiles/ (decode B=64 launch; prefill at T=8192).
 # decode: 33.83 MB read; the 33.55 MB of state writes are still dirty in L2 when ncu's replayed launch ends.
-# prefill_8k_call: the four launches of one default-route call (prep 59.9 MB, segment-local 87.0, chain 7.6,
+# prefill_8k_call: the four launches of one default-route call (prep 60.0 MB, segment-local 88.1, chain 7.6,
 # output 52.8), each measured with ncu's per-kernel cache flush.
-NCU_TRAFFIC = {"decode": 33832960, "prefill_8k_call": 207338155}
+NCU_TRAFFIC = {"decode": 33832960, "prefill_8k_call": 208500000}
 
 
 def env_int(name, default):
