@@ -752,6 +752,26 @@ def main():
             ev1.record()
             barrier()
             out[name] = round(reps * nbytes / (ev0.elapsed_time(ev1) * 1e-3) / 1e9, 2)
+        # both directions at once on two streams (what the pipelined e2e loop does), every rank at once:
+        # the sum over ranks of bidir_GBps is the host-side throughput the whole box reached
+        hb2 = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        db2 = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        s_a, s_b = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        cur = torch.cuda.current_stream(dev)
+        barrier()
+        ev0.record()
+        s_a.wait_stream(cur)
+        s_b.wait_stream(cur)
+        for _ in range(reps):
+            with torch.cuda.stream(s_a):
+                db.copy_(hb, non_blocking=True)
+            with torch.cuda.stream(s_b):
+                hb2.copy_(db2, non_blocking=True)
+        cur.wait_stream(s_a)
+        cur.wait_stream(s_b)
+        ev1.record()
+        barrier()
+        out["bidir_GBps"] = round(2 * reps * nbytes / (ev0.elapsed_time(ev1) * 1e-3) / 1e9, 2)
         return out
 
     e2e = None
