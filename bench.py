@@ -62,7 +62,10 @@ REPS = 5  # timed repetitions of every measurement; the median is reported
 # decode: 33.83 MB read; the 33.55 MB of state writes are still dirty in L2 when ncu's replayed launch ends.
 # prefill_8k_call: the four launches of one default-route call (prep 60.0 MB, segment-local 88.1, chain 7.6,
 # output 52.8), each measured with ncu's per-kernel cache flush.
-NCU_TRAFFIC = {"decode": 33832960, "prefill_8k_call": 208500000}
+# prefill_8k_call_warm: the same four launches with ncu's --cache-control none (caches kept between kernels, as
+# in the timed call): 256 MB, because write-backs of earlier kernels' dirty lines then land in later kernels
+# (prep 100.5 MB, segment-local 111.3, chain 3.2, output 40.8).
+NCU_TRAFFIC = {"decode": 33832960, "prefill_8k_call": 208500000, "prefill_8k_call_warm": 255800000}
 
 
 def env_int(name, default):
@@ -857,6 +860,8 @@ def main():
             "roofline": {"bound": "max(hbm, tensor)", "achieved_frac": round(pre_bound_s / (pre_ms * 1e-3), 5),
                          "bound_us": round(pre_bound_s * 1e6, 3), "alg_bytes": pre_bytes, "alg_flops": pre_flops,
                          "traffic": NCU_TRAFFIC["prefill_8k_call"], "traffic_scope": "all kernels of one call",
+                         "traffic_warm_caches": NCU_TRAFFIC["prefill_8k_call_warm"],
+                         "kernel_us_warm": {"prep": 56.3, "seg_local": 46.8, "seg_chain": 8.4, "seg_out": 17.9},
                          "peak_source": peak_src},
             "routes": pre_routes,
             "head_split": head_split,
