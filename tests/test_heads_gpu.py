@@ -81,3 +81,25 @@ def test_prefill_head_split_of_reference_family(world, lens):
     import numpy as np
     util.check_out(np.concatenate(outs, axis=1), ro)
     util.check_state(np.concatenate(states, axis=1), rs)
+
+
+def test_prefill_head_split_l2norm_int64_cu():
+    """The 4-way head split pieces (1 q/k head, 2 v-heads each) with the in-kernel L2 norm and int64 cu_seqlens,
+    on a batch of mixed lengths (6144 tokens down to 1)."""
+    from gdn.shard import head_shard
+
+    inp = gi.prefill_inputs([6144, 40, 1, 700], seed=931, normalized=False)
+    ro, rs = oracle.prefill(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"],
+                            inp["b"], inp["cu_seqlens"], inp["scale"], qk_l2norm=True)
+    import numpy as np
+    outs, states = [], []
+    for r in range(4):
+        h0, h1, v0, v1 = head_shard(4, 8, 4, r, prefill=True)
+        part = dict(inp, q=inp["q"][:, h0:h1], k=inp["k"][:, h0:h1], v=inp["v"][:, v0:v1], state=inp["state"][:, v0:v1],
+                    A_log=inp["A_log"][v0:v1], a=inp["a"][:, v0:v1], dt_bias=inp["dt_bias"][v0:v1], b=inp["b"][:, v0:v1])
+        o, ns = gdn.prefill.run(*util.prefill_args(part, cu_dtype=torch.int64), use_qk_l2norm_in_kernel=True)
+        outs.append(util.bits(o))
+        states.append(ns.cpu().numpy())
+    torch.cuda.synchronize()
+    util.check_out(np.concatenate(outs, axis=1), ro)
+    util.check_state(np.concatenate(states, axis=1), rs)
