@@ -267,9 +267,9 @@ def test_prefill_bounded_wait_reports_and_recovers(scan):
     util.check_state(ns.cpu().numpy(), rs)
 
 
-@pytest.mark.parametrize("lens", [[6] * 40, [1, 2, 3, 32, 0, 33, 5, 4] * 6, [1, 24, 25, 3, 200, 0, 17] * 6,
-                                  [24] * 33, list(range(33)) + [40, 64, 65]],
-                         ids=["40x6", "rec_mixed", "mixed", "33x24", "tc_0to32"])
+@pytest.mark.parametrize("lens", [[6] * 40, [1, 2, 3, 32, 0, 33, 5, 4] * 6, [8, 9, 16, 17, 1, 2, 3, 4] * 6,
+                                  [1, 24, 25, 3, 200, 0, 17] * 6, [24] * 33, list(range(33)) + [40, 64, 65]],
+                         ids=["40x6", "rec_mixed", "rec_block_edges", "mixed", "33x24", "tc_0to32"])
 def test_prefill_short_sequence_path(lens):
     """In batches of more than 32 sequences, sequences of up to 32 tokens take a short-sequence
     kernel (the token recurrence when the batch averages at most 10 tokens per sequence, the
