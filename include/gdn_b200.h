@@ -145,8 +145,9 @@ size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV, int K, int V);
  *               required even when T == 0; no contents are carried between calls.  Its first
  *               int receives 0, or the code of a bounded device-side wait that gave up
  *               (the call's outputs are then invalid); reading it is optional.
- * Pointers to q, k, v, a, b, state, out, new_state must be 16-byte aligned (the kernels read
- * q, k, v, a and b with TMA tile copies).
+ * Pointers to q, k, v, state, out, new_state must be 16-byte aligned (the kernels read q, k, v
+ * with TMA tile copies); a and b too when HV is a multiple of 8 (then also TMA tiles), else
+ * 2-byte aligned.
  * Sequence bounds are clamped to [0, T] on the device, so malformed cu_seqlens
  * cannot make the kernels read or write outside the buffers.
  */
