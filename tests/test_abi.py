@@ -127,3 +127,15 @@ def test_scale_resolution():
     assert resolve_scale(0.0) == pytest.approx(1 / math.sqrt(128))
     assert resolve_scale(torch.tensor(0.5)) == 0.5
     assert resolve_scale(2) == 2.0
+
+
+def test_prefill_gate_pointer_alignment_depends_on_head_count(lib):
+    """a and b are TMA tiles (16-byte aligned) when HV is a multiple of 8, plain bf16 loads (2-byte
+    aligned) otherwise; the check runs before any device work, so no GPU is needed."""
+    def call(gate_ptr, H, HV):
+        p = 256
+        return lib.gdn_prefill_fwd(p, p, p, None, p, gate_ptr, p, gate_ptr, p, 0, 1, 64, 1.0, p, p, 256, 1 << 30,
+                                   H, HV, 128, 128, None, 0)
+    assert call(258, 4, 8) == 3   # 8 v-heads: gate tiles need 16-byte alignment
+    assert call(258, 1, 2) != 3   # 2 v-heads: 2-byte alignment is enough
+    assert call(257, 1, 2) == 3   # but not an odd address
