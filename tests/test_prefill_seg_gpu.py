@@ -127,3 +127,27 @@ def test_segmented_route_is_the_default_for_long_sequences():
     o2, s2 = _call(inp, SEGMENTS)
     assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
     assert torch.equal(s1.view(torch.int32), s2.view(torch.int32))
+
+
+@pytest.mark.parametrize("h,hv", [(1, 2), (1, 1), (2, 4)], ids=["qk1_v2", "qk1_v1", "qk2_v4"])
+@pytest.mark.parametrize("lens", [[3000, 700, 64, 1], [6500]], ids=["mixed4", "6500"])
+def test_segmented_prefill_few_v_heads(h, hv, lens):
+    """The segmented route with the few v-heads of one head-split piece (its segment length then comes
+    from the lower bound m^2 >= chunks / 3), forced on several sequences and taken by default on one
+    long sequence, against the oracle and the single-pass scan."""
+    inp = gi.prefill_inputs(lens, seed=1300 + h + hv + len(lens), h=h, hv=hv)
+    args = util.prefill_args(inp)
+    T, N = args[0].shape[0], args[8].shape[0] - 1
+    outs = []
+    for flags in (SEGMENTS, NO_SEGMENTS):
+        out = torch.empty(T, hv, 128, dtype=torch.bfloat16, device="cuda")
+        ns = torch.empty(N, hv, 128, 128, dtype=torch.float32, device="cuda")
+        ws = torch.empty(gdn.prefill.workspace_bytes(N, T, h, hv), dtype=torch.uint8, device="cuda")
+        pmod._launch(*args, out, ns, workspace=ws, flags=flags)
+        torch.cuda.synchronize()
+        assert gdn.prefill.read_status(ws) == 0
+        outs.append((out, ns))
+    ro, rs = _oracle(inp)
+    for out, ns in outs:
+        util.check_out(util.bits(out), ro)
+        util.check_state(ns.cpu().numpy(), rs)
