@@ -133,8 +133,8 @@ def test_segmented_route_is_the_default_for_long_sequences():
 @pytest.mark.parametrize("lens", [[3000, 700, 64, 1], [6500]], ids=["mixed4", "6500"])
 def test_segmented_prefill_few_v_heads(h, hv, lens):
     """The segmented route with the few v-heads of one head-split piece (its segment length then comes
-    from the lower bound m^2 >= chunks / 3), forced on several sequences and taken by default on one
-    long sequence, against the oracle and the single-pass scan."""
+    from the lower bound m^2 >= chunks / 3) and the single-pass scan on the same inputs, both against the
+    oracle, for several sequences and for one long one."""
     inp = gi.prefill_inputs(lens, seed=1300 + h + hv + len(lens), h=h, hv=hv)
     args = util.prefill_args(inp)
     T, N = args[0].shape[0], args[8].shape[0] - 1
