@@ -278,8 +278,11 @@ def profile_run(args):
     g = torch.Generator(device=dev).manual_seed(0)
     rn = lambda *sh: torch.randn(*sh, generator=g, device=dev)
     l2n = lambda x: (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
-    A_log = torch.rand(HV, generator=g, device=dev) * math.log(16.0)
-    dt_bias = rn(HV) * 0.1
+    # prefill may take other head counts (N,T,FLAGS,H,HV): e.g. the pieces of a head split
+    parts = [int(x, 0) for x in args.profile_prefill.split(",")] if args.profile_prefill else []
+    nh, nhv = (parts[3], parts[4]) if len(parts) > 4 else (H, HV)
+    A_log = torch.rand(nhv, generator=g, device=dev) * math.log(16.0)
+    dt_bias = rn(nhv) * 0.1
     if args.profile_decode:
         B = args.profile_decode
         q, k = l2n(rn(B, 1, H, D)), l2n(rn(B, 1, H, D))
@@ -289,16 +292,15 @@ def profile_run(args):
         for _ in range(3):
             gdn.decode.kernel(q, k, v, st, A_log, a, dt_bias, b, D ** -0.5, out, st)
     else:
-        parts = [int(x, 0) for x in args.profile_prefill.split(",")]
         N, T, flags = parts[0], parts[1], (parts[2] if len(parts) > 2 else 0)
         TT = N * T
-        q, k = l2n(rn(TT, H, D)), l2n(rn(TT, H, D))
-        v, a, b = rn(TT, HV, D).bfloat16(), rn(TT, HV).bfloat16(), rn(TT, HV).bfloat16()
-        h0 = rn(N, HV, D, D) * 0.02
+        q, k = l2n(rn(TT, nh, D)), l2n(rn(TT, nh, D))
+        v, a, b = rn(TT, nhv, D).bfloat16(), rn(TT, nhv).bfloat16(), rn(TT, nhv).bfloat16()
+        h0 = rn(N, nhv, D, D) * 0.02
         cu = torch.arange(N + 1, dtype=torch.int32, device=dev) * T
-        out = torch.empty(TT, HV, D, dtype=torch.bfloat16, device=dev)
-        ns = torch.empty(N, HV, D, D, device=dev)
-        ws = torch.empty(gdn.prefill.workspace_bytes(N, TT), dtype=torch.uint8, device=dev)
+        out = torch.empty(TT, nhv, D, dtype=torch.bfloat16, device=dev)
+        ns = torch.empty(N, nhv, D, D, device=dev)
+        ws = torch.empty(gdn.prefill.workspace_bytes(N, TT, nh, nhv), dtype=torch.uint8, device=dev)
         for _ in range(3):
             pmod._launch(q, k, v, h0, A_log, a, dt_bias, b, cu, D ** -0.5, out, ns, workspace=ws, flags=flags)
     torch.cuda.synchronize()
@@ -314,9 +316,10 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--profile-prefill", metavar="N,T[,FLAGS]", default=None,
+    ap.add_argument("--profile-prefill", metavar="N,T[,FLAGS[,H,HV]]", default=None,
                     help="profiling aid (ncu): run 3 prefill calls of N sequences x T tokens (library flags, "
-                         "e.g. 0x8 for the single-pass scan) and exit; prints no JSON line")
+                         "e.g. 0x8 for the single-pass scan; optional head counts, e.g. 1,2 for a piece of a "
+                         "4-way head split) and exit; prints no JSON line")
     ap.add_argument("--profile-decode", metavar="B", type=int, default=None,
                     help="profiling aid (ncu): run 3 decode steps at batch B and exit")
     args = ap.parse_args()
