@@ -427,8 +427,8 @@ constexpr uint32_t kOffD = 0;         // D: 2 atoms of [128 rows][128 B], SW128
 constexpr uint32_t kOffB = 32768;     // B slice [128][8] f32
 constexpr uint32_t kStage = 32768 + 4096;
 constexpr uint32_t kTx = 32768 + 4096;
-constexpr uint32_t kOffHb = kStages * kStage;       // h bf16 [128][8]
-constexpr uint32_t kOffBar = kOffHb + 128 * kHS * 2;
+constexpr uint32_t kOffHb = kStages * kStage;       // h bf16 [2][128][8]: step s reads copy s % 2
+constexpr uint32_t kOffBar = kOffHb + 2 * 128 * kHS * 2;
 constexpr uint32_t kSmemUsed = kOffBar + 16 * kStages + 16;
 constexpr uint32_t kSmem = kSmemUsed + 1024;
 }  // namespace segc
@@ -497,23 +497,33 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
             h[e] = st_in ? st_in[(size_t)(v0 + col) * kD + row] : 0.f;
         }
     }
-    int s = 0;
-    for (; s < nseg; ++s) {
-        // h_s (bf16): this step's MMA operand and the output kernel's
-        const size_t seg_i = (size_t)hv * p.SS + sq.sbase + s;
+    // h_s (bf16) into copy s % 2 of Hb (this step's MMA operand) and into the workspace (the output
+    // kernel's operand).  Two copies: a warp writes copy (s + 1) % 2 at the end of step s while
+    // others may still read copy s % 2, and no warp reaches step s + 2's write before every warp has
+    // passed step s + 1's barrier, i.e. finished reading copy s % 2 -- one barrier per step.
+    auto put_h = [&](int step) {
+        uint16_t* hb = Hb + (step & 1) * 128 * kHS;
+        const size_t seg_i = (size_t)hv * p.SS + sq.sbase + step;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int row = 16 * mw + gq + 8 * hh;
             const uint32_t pk = pack_bf16x2(h[2 * hh], h[2 * hh + 1]);
-            *reinterpret_cast<uint32_t*>(Hb + row * kHS + 2 * tq) = pk;
+            *reinterpret_cast<uint32_t*>(hb + row * kHS + 2 * tq) = pk;
             *reinterpret_cast<uint32_t*>(p.seg_hb + (seg_i * 128 + row) * 128 + v0 + 2 * tq) = pk;
         }
+    };
+    int s = 0;
+    float gam = nseg > 0 ? p.seg_gamma[(size_t)hv * p.SS + sq.sbase] : 0.f;
+    if (nseg > 0) put_h(0);
+    for (; s < nseg; ++s) {
         if (!mbar_wait(full + (s % kStages), (uint32_t)((s / kStages) & 1), p.status, kErrScanTmaTimeout))
             *abort_flag = 1;
-        named_bar_sync(1, kMath);
+        named_bar_sync(1, kMath);  // copy s % 2 of Hb is complete
         if (*abort_flag) break;
         const unsigned char* st = sm + (s % kStages) * kStage;
-        const float gam = p.seg_gamma[seg_i];
+        const uint16_t* hb = Hb + (s & 1) * 128 * kHS;
+        // the next segment's gamma, a step ahead (a global load otherwise on the serial path)
+        const float gam_next = s + 1 < nseg ? p.seg_gamma[(size_t)hv * p.SS + sq.sbase + s + 1] : 0.f;
         // P = D h_s for rows 16 mw .. +15 (even / odd k-steps in separate accumulators)
         float pa[4] = {0.f, 0.f, 0.f, 0.f}, pb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -522,7 +532,7 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
             ldsm_x4(a[0], a[1], a[2], a[3], st + kOffD + sw128_off(16 * mw + (lane & 15), k0 + ((lane >> 4) << 3), 16384));
             asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
                          : "=r"(b0), "=r"(b1)
-                         : "r"(smem_u32(Hb + (k0 + (lane & 15)) * kHS)));
+                         : "r"(smem_u32(hb + (k0 + (lane & 15)) * kHS)));
             if ((k0 >> 4) & 1)
                 mma_bf16(pb, a, b0, b1);
             else
@@ -534,9 +544,10 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
             const int row = 16 * mw + gq + 8 * (e >> 1), col = 2 * tq + (e & 1);
             h[e] = fmaf(gam, h[e], pa[e] + pb[e] + Bs[row * 8 + col]);
         }
+        gam = gam_next;
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + (s % kStages));
-        named_bar_sync(1, kMath);  // every warp has read Hb before it is rewritten
+        if (s + 1 < nseg) put_h(s + 1);
     }
     if (s < nseg) {
         if (tid == 0)
