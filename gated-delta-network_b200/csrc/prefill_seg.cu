@@ -136,8 +136,9 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
         tma_prefetch_desc(&maps.k);
         tma_prefetch_desc(half ? &maps.qpp : &maps.oipp);
     }
-    pdl_wait();  // the workspace comes from the prep kernel
-    pdl_trigger();
+    // Set-up that reads no prep output runs before the grid-dependency wait, overlapping the prep's
+    // tail: the segment lookup (cu_seqlens was complete before the prep started its work), the
+    // barriers and the TMEM allocation (no prep CTA shares an SM with this 200 KB CTA).
     const SegSeq sq = warp_seg_seq(p, kBySeg, ss);
     if (sq.n < 0 || ss >= p.SS) return;  // a slot past the last segment (uniform across the CTA)
     int bos, eos;
@@ -164,6 +165,8 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    pdl_wait();  // the workspace comes from the prep kernel
+    pdl_trigger();
 
     if (warp == kMath / 32) {
         // Producer: stage c % 2 gets chunk c's W, Q', K tiles, gates and (half 0) u once chunk
@@ -447,13 +450,16 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
     const int gq = lane >> 2, tq = lane & 3;
     const int v0 = blockIdx.x * BV, n = blockIdx.y, hv = blockIdx.z;
     if (warp == kMath / 32 && lane == 0) tma_prefetch_desc(&maps.segD);
-    pdl_wait();  // the segment transitions come from the local kernel
-    pdl_trigger();
+    // Set-up that reads no output of the segment kernels runs before the grid-dependency wait, over
+    // the local kernel's tail: the sequence lookup, the barriers and the initial state (inputs that
+    // were complete before the prep started its work; no earlier kernel of this call writes them).
     const SegSeq sq = warp_seg_seq(p, kBySeq, n);
     int bos, eos;
     seq_bounds(p.cu, p.cu64, n, p.T, bos, eos);
     float* st_out = p.new_state + ((size_t)n * p.HV + hv) * kD * kD;
     if (eos - bos <= 0) {  // zero-length sequence: all-zero final state (reference/gdn_prefill_ref.py:52-54, 61-62)
+        pdl_wait();
+        pdl_trigger();
         for (int idx = tid; idx < BV * kD; idx += kThreads) st_out[(size_t)(v0 + idx / kD) * kD + idx % kD] = 0.f;
         return;
     }
@@ -469,6 +475,19 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
         mbar_fence_init();
     }
     __syncthreads();
+    // math warp mw owns state rows 16 mw .. 16 mw + 15: h[e] = h[16 mw + gq + 8 (e >> 1)][2 tq + (e & 1)]
+    const int mw = warp;
+    float h[4];
+    if (warp < kMath / 32) {
+        const float* st_in = p.state ? p.state + ((size_t)n * p.HV + hv) * kD * kD : nullptr;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int row = 16 * mw + gq + 8 * (e >> 1), col = 2 * tq + (e & 1);
+            h[e] = st_in ? st_in[(size_t)(v0 + col) * kD + row] : 0.f;
+        }
+    }
+    pdl_wait();  // the segment transitions come from the local kernel
+    pdl_trigger();
     if (warp == kMath / 32) {
         if (lane == 0) {
             for (int s = 0; s < nseg; ++s) {
@@ -485,17 +504,6 @@ __global__ void __launch_bounds__(segc::kThreads, 1)
             }
         }
         return;
-    }
-    // math warp mw owns state rows 16 mw .. 16 mw + 15: h[e] = h[16 mw + gq + 8 (e >> 1)][2 tq + (e & 1)]
-    const int mw = warp;
-    float h[4];
-    {
-        const float* st_in = p.state ? p.state + ((size_t)n * p.HV + hv) * kD * kD : nullptr;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int row = 16 * mw + gq + 8 * (e >> 1), col = 2 * tq + (e & 1);
-            h[e] = st_in ? st_in[(size_t)(v0 + col) * kD + row] : 0.f;
-        }
     }
     // h_s (bf16) into copy s % 2 of Hb (this step's MMA operand) and into the workspace (the output
     // kernel's operand).  Two copies: a warp writes copy (s + 1) % 2 at the end of step s while
@@ -625,11 +633,9 @@ __global__ void __launch_bounds__(sego::kThreads, 1)
         tma_prefetch_desc(&maps.oipp);
         tma_prefetch_desc(&maps.seghb);
     }
-    pdl_wait();
-    pdl_trigger();
-    if (blockIdx.x == 0 && warp < kEpi / 32) zero_unowned_tokens(p, tid, kEpi);
     const int npair = (p.seg_m + kPair - 1) / kPair;
     const int total = p.SS * p.HV * npair;
+    // barriers and TMEM before the grid-dependency wait (no chain CTA shares an SM with this one)
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
             mbar_init(full + b, 1);
@@ -644,6 +650,9 @@ __global__ void __launch_bounds__(sego::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    pdl_wait();
+    pdl_trigger();
+    if (blockIdx.x == 0 && warp < kEpi / 32) zero_unowned_tokens(p, tid, kEpi);
     OutItem it;
     if (warp == kProdWarp) {
         int i = 0;
