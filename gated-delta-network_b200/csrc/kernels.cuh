@@ -112,10 +112,13 @@ __host__ __device__ constexpr int prefill_seg_m(int N, int T, int HV) {
     return 0;
 }
 // Whether a call takes the segmented route by default (it still needs prefill_seg_m > 0).
-// Measured on B200 (one sequence): 8192 tokens 139 us against 159 us for the single-pass scan,
-// 4096 tokens even (84 / 85 us), shorter sequences slower; so sequences averaging at least
-// 6144 tokens.
-__host__ __device__ constexpr bool prefill_seg_default(int N, int T) { return N >= 1 && T >= 6144LL * N; }
+// Measured on B200 (segmented / single-pass scan): one sequence of 8192 tokens 127 / 157 us,
+// 4096 76 / 85 us, 3072 68 / 71 us, 2048 49 / 48 us; two sequences of 4096 even (129 / 128 us),
+// of 2048 78 / 72 us; four of 2048 150 / 116 us.  So one sequence of at least 3072 tokens, or
+// sequences averaging at least 6144.
+__host__ __device__ constexpr bool prefill_seg_default(int N, int T) {
+    return N >= 1 && (T >= 6144LL * N || (N == 1 && T >= 3072));
+}
 __host__ __device__ constexpr PrefillLayout prefill_layout(int N, int T, int HV = 8) {
     PrefillLayout L{};
     long long S = (long long)T / 64 + N;

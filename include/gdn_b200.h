@@ -55,9 +55,9 @@ enum gdn_status {
  * norm of the reference's decode sweep kernel, tests/bench_decode_sweep.py:43-46, and of FLA's
  * use_qk_l2norm_in_kernel).  Without it q and k are used as given, as the reference oracles do. */
 #define GDN_FLAG_QK_L2NORM 0x4u
-/* Prefill route.  By default calls of a few sequences averaging at least 6144 tokens split every
- * sequence into segments whose state transitions are built in parallel and then chained
- * (gdn_prefill_fwd decides from N and T).  GDN_FLAG_NO_SEGMENTS keeps the single-pass recurrence;
+/* Prefill route.  By default a call of one sequence of at least 3072 tokens, or of a few sequences
+ * averaging at least 6144 tokens, splits every sequence into segments whose state transitions are
+ * built in parallel and then chained (gdn_prefill_fwd decides from N and T).  GDN_FLAG_NO_SEGMENTS keeps the single-pass recurrence;
  * GDN_FLAG_SEGMENTS takes the segmented route for any call whose workspace has its regions (at most
  * 32 sequences averaging at least 512 tokens, see gdn_prefill_workspace_bytes).  Bits 16-23
  * (value << 16) force the segment length in 64-token chunks (it must not need more segment slots

@@ -1,5 +1,5 @@
 """The segmented prefill route (csrc/prefill_seg.cu) against the CPU oracle and against the
-single-pass scan.  Calls of a few sequences averaging >= 6144 tokens take it by default;
+single-pass scan.  One sequence of >= 3072 tokens, or a few averaging >= 6144, take it by default;
 GDN_FLAG_SEGMENTS forces it for the other calls whose workspace has its regions,
 GDN_FLAG_NO_SEGMENTS forces the single-pass scan, and bits 16-23 force a segment length.  Cases cover one sequence, several, ragged tails, a one-token and a
 zero-length sequence, and segment lengths that do and do not divide the chunk count."""
