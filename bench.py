@@ -31,6 +31,7 @@ a MAX all-reduce of the timings only.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -530,13 +531,18 @@ def main():
                for _ in range(args.prefill_steps)]
         for e0, e1 in evs:
             flush_l2(clean)
-            torch.cuda._sleep(200_000)  # keeps the GPU busy while the host submits the call
+            torch.cuda._sleep(2_000_000)  # ~1 ms: the GPU stays busy while the host submits the call
             e0.record()
             prefill_step(flags)
             e1.record()
         barrier()
         return max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs))
 
+    # Host-side pauses (the interpreter's garbage collector in this large process) inside a timed
+    # region would leave the GPU idle between a call's launches: collection is off while the prefill
+    # sections run, and each timed call is queued behind a ~1 ms sleep kernel.
+    gc.collect()
+    gc.disable()
     pre_ms = time_8k(0)  # the library's default route (segmented for one 8192-token sequence)
 
     # the same sequence split by v-head over the ranks (gdn.shard.head_shard: each rank runs its q/k
@@ -562,7 +568,7 @@ def main():
                for _ in range(args.prefill_steps)]
         for e0, e1 in evs:
             flush_l2()
-            torch.cuda._sleep(200_000)
+            torch.cuda._sleep(2_000_000)
             e0.record()
             step()
             e1.record()
@@ -600,7 +606,7 @@ def main():
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         for e0, e1 in evs:
             flush_l2()
-            torch.cuda._sleep(200_000)  # keeps the GPU busy while the host submits the call
+            torch.cuda._sleep(2_000_000)  # ~1 ms: the GPU stays busy while the host submits the call
             e0.record()
             step()
             e1.record()
@@ -671,6 +677,7 @@ def main():
         "method": "median of 20 iterations; each clones all 11 tensor arguments, then calls gdn.prefill.kernel, "
                   "both inside the CUDA-event region (FlashInfer-Bench do_bench _clone_args)",
     }
+    gc.enable()
 
     # ---------------- e2e through the public API with pinned host buffers ----------------
     # Every step copies its inputs host -> device from pinned memory, runs the public call and
