@@ -38,8 +38,9 @@ GDN_DBG_READER(gdn_debug_read_seg)
 namespace gdn {
 
 namespace segk {
-constexpr int kThreads = 544;  // 16 math warps (four per TMEM lane quarter) + 1 TMA producer warp
+constexpr int kThreads = 512;  // 16 math warps (four per TMEM lane quarter); thread kIssuer also issues the TMA
 constexpr int kMath = 512;
+constexpr int kIssuer = 96;    // warp 3, lane 0: an output-row warp, off the chain's critical path
 constexpr int kCW = 32;        // state columns per math thread
 constexpr int kStages = 2;
 constexpr uint32_t kOffWQ = 0;          // [W0 | Q'0 | W1 | Q'1], 8 KB each; after MMA_P: output staging
@@ -50,7 +51,7 @@ constexpr uint32_t kStage = 82944;      // 81 KB (1024-aligned)
 constexpr uint32_t kTxTiles = 6 * 8192 + 1024;
 constexpr uint32_t kOffX = kStages * kStage;   // X bf16, 2 column blocks of [128 rows][128 B], SW128;
                                                // between MMA_P and MMA_U: vn hi / lo [2][64][128 B] each
-constexpr uint32_t kOffBar = kOffX + 32768;    // full[2], empty[2], mma_p, mma_u
+constexpr uint32_t kOffBar = kOffX + 32768;    // full[2], (unused)[2], mma_p, mma_u
 constexpr uint32_t kSmemUsed = kOffBar + 8 * 6 + 16;
 constexpr uint32_t kSmem = kSmemUsed + 1024;
 constexpr uint32_t kTmemCols = 256;            // P: 0-127, D: 128-255
@@ -112,8 +113,8 @@ __device__ __forceinline__ SegSeq warp_seg_seq(const PrefillArgs& p, int kind, i
 // ------------------------------------------------------------------------------------------
 // 1. local transitions
 // ------------------------------------------------------------------------------------------
-// 544 threads: registers are granted to warps in groups of four, so 20 warps' worth of the
-// 64 K-entry file caps this kernel at 96 registers per thread
+// 512 threads, 16 warps: the whole 64 K-entry register file gives 128 registers per thread.  A
+// separate producer warp (17 warps, granted as 20) would cap them at 96 and spill.
 __global__ void __launch_bounds__(segk::kThreads, 1)
     gdn_prefill_seg_local_kernel(PrefillArgs p, const __grid_constant__ PrefillMaps maps) {
     using namespace segk;
@@ -121,8 +122,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(sm);
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);
-    uint64_t* empty = full + kStages;
-    uint64_t* bar_p = empty + kStages;
+    uint64_t* bar_p = full + 2 * kStages;
     uint64_t* bar_u = bar_p + 1;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_u + 1);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_u + 1) + 1;
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ss = blockIdx.x, hv = blockIdx.y, half = blockIdx.z;  // half 0: beta (with u), 1: Phi
     const int hq = hv / (p.HV / p.H);
-    if (warp == kMath / 32 && lane == 0) {
+    if (tid == kIssuer) {
         tma_prefetch_desc(&maps.w);
         tma_prefetch_desc(&maps.qp);
         tma_prefetch_desc(&maps.k);
@@ -151,10 +151,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
     const int slot0 = sq.cbase + c0;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(full + s, 1);
-            mbar_init(empty + s, kMath / 32);
-        }
+        for (int s = 0; s < kStages; ++s) mbar_init(full + s, 1);
         mbar_init(bar_p, 1);
         mbar_init(bar_u, 1);
         *abort_flag = 0;
@@ -168,29 +165,29 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
     pdl_wait();  // the workspace comes from the prep kernel
     pdl_trigger();
 
-    if (warp == kMath / 32) {
-        // Producer: stage c % 2 gets chunk c's W, Q', K tiles, gates and (half 0) u once chunk
-        // c - 2 is done.
-        if (lane == 0) {
-            for (int c = 0; c < nch; ++c) {
-                if (c >= kStages && !mbar_wait(empty + (c % kStages), (uint32_t)((c / kStages - 1) & 1), p.status,
-                                               kErrScanTmaTimeout))
-                    break;
-                unsigned char* st = sm + (c % kStages) * kStage;
-                uint64_t* bar = full + (c % kStages);
-                const int slot = slot0 + c, wr = slot * kChunk, t0 = bos + (c0 + c) * kChunk;
-                mbar_arrive_expect_tx(bar, kTxTiles + (half == 0 ? 32768u : 0u));
-                tma_load_3d(st + kOffWQ, &maps.w, 0, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 8192, &maps.qp, 0, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 16384, &maps.w, 64, wr, hv, bar);
-                tma_load_3d(st + kOffWQ + 24576, &maps.qp, 64, wr, hv, bar);
-                tma_load_3d(st + kOffK, &maps.k, 0, hq, t0, bar);
-                tma_load_3d(st + kOffK + 8192, &maps.k, 64, hq, t0, bar);
-                bulk_load(st + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, bar);
-                if (half == 0) bulk_load(st + kOffU, p.u + cg_off(hv, p.S, slot, 0), 32768, bar);
-            }
-        }
-    } else {
+    // Chunk c's W, Q', K tiles, gates and (half 0) u go to stage c % 2, issued by thread kIssuer:
+    // chunks 0 and 1 here, chunk c + 1 at the top of chunk c once the barrier there shows that every
+    // thread is done with chunk c - 1, the stage's previous contents (its output tile read by the
+    // TMA store included).  n_issued counts the chunks issued (kIssuer's own count).
+    int n_issued = 0;
+    auto issue = [&](int c) {
+        unsigned char* st = sm + (c % kStages) * kStage;
+        uint64_t* bar = full + (c % kStages);
+        const int slot = slot0 + c, wr = slot * kChunk, t0 = bos + (c0 + c) * kChunk;
+        mbar_arrive_expect_tx(bar, kTxTiles + (half == 0 ? 32768u : 0u));
+        tma_load_3d(st + kOffWQ, &maps.w, 0, wr, hv, bar);
+        tma_load_3d(st + kOffWQ + 8192, &maps.qp, 0, wr, hv, bar);
+        tma_load_3d(st + kOffWQ + 16384, &maps.w, 64, wr, hv, bar);
+        tma_load_3d(st + kOffWQ + 24576, &maps.qp, 64, wr, hv, bar);
+        tma_load_3d(st + kOffK, &maps.k, 0, hq, t0, bar);
+        tma_load_3d(st + kOffK + 8192, &maps.k, 64, hq, t0, bar);
+        bulk_load(st + kOffG, p.g4 + ((size_t)hv * p.S + slot) * kChunk * 4, 1024, bar);
+        if (half == 0) bulk_load(st + kOffU, p.u + cg_off(hv, p.S, slot, 0), 32768, bar);
+        n_issued = c + 1;
+    };
+    if (tid == kIssuer)
+        for (int c = 0; c < min(nch, kStages); ++c) issue(c);
+    {
         // ---- math warps: thread (r, cq) = TMEM lane r, state columns cb = kCW cq .. cb + kCW - 1 ----
         // (warps w, w + 4, w + 8, w + 12 share TMEM lane quarter w and split its columns)
         const int r = lane + 32 * (warp & 3), cq = warp >> 2;
@@ -218,6 +215,7 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
             named_bar_sync(1, kMath);
             GDN_PH_ACC(dbg, 1, tp);
             if (*abort_flag) break;  // written only before this barrier
+            if (tid == kIssuer && c >= 1 && c + 1 < nch) issue(c + 1);
             tc_fence_after();
             const unsigned char* st = sm + (c % kStages) * kStage;
             const uint32_t sst = sbase + (uint32_t)(c % kStages) * kStage;
@@ -375,16 +373,14 @@ __global__ void __launch_bounds__(segk::kThreads, 1)
             }
             // the stage's operands are consumed (and its output tile read by the TMA store)
             if (tid == 64) tma_store_wait_read();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty + (c % kStages));
             if (!ok) *abort_flag = 1;
             GDN_SEG_WRITE_XB();
             GDN_PH_ACC(dbg, 7, tp);
         }
         if (c < nch) {
             // gave up: let copies already in flight land (bounded) before the CTA exits
-            if (tid == 0)
-                for (int cc = c + 1; cc < min(nch, c + kStages); ++cc)
+            if (tid == kIssuer)
+                for (int cc = c; cc < n_issued; ++cc)
                     mbar_wait(full + (cc % kStages), (uint32_t)((cc / kStages) & 1), nullptr, 0);
         } else {
             const size_t seg_i = (size_t)hv * p.SS + ss;
