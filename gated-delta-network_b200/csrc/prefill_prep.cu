@@ -379,8 +379,11 @@ __global__ void __launch_bounds__(prep2::kThreads, 2)
                     for (int Jh = 0; Jh < 2; ++Jh) {
                         const int J = 2 * half + Jh;
                         if (J < I) {
+                            // J depends on the runtime column half: pick the factor by compares, so aJ stays
+                            // in registers (an indexed read would place it in local memory)
+                            const float a = J == 0 ? aJ[0] : (J == 1 ? aJ[1] : aJ[2]);
 #pragma unroll
-                            for (int c = 0; c < 16; ++c) v[16 * Jh + c] = aJ[J < 3 ? J : 2] * Bt[16 * J + c] * d[16 * Jh + c];
+                            for (int c = 0; c < 16; ++c) v[16 * Jh + c] = a * Bt[16 * J + c] * d[16 * Jh + c];
                         } else if (J == I) {
 #pragma unroll
                             for (int c = 0; c < 16; ++c) {
