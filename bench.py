@@ -68,10 +68,10 @@ REPS = 5  # timed repetitions of every measurement; the median is reported
 # (prep 100.5 MB, segment-local 111.3, chain 3.2, output 40.8).
 NCU_TRAFFIC = {"decode": 33832960, "prefill_8k_call": 208500000, "prefill_8k_call_warm": 255800000}
 # Critical path of the 8K call with the current kernels given unlimited SMs (us): one prep item (~11), the local
-# chain of one segment (15 chunk steps x ~3.1), the chain over 9 segments (~0.93 each) and one output item (~5),
+# chain of one segment (15 chunk steps x ~2.95), the chain over 9 segments (~0.92 each) and one output item (~5),
 # from the phase counters and the warm launch list.  The remaining time of the call is throughput: the prep's
 # 1024 (chunk, v-head) items take 3.5 waves of two CTAs per SM.
-PREFILL_8K_CRITICAL_PATH_US = 71.0
+PREFILL_8K_CRITICAL_PATH_US = 68.5
 
 
 def env_int(name, default):
@@ -876,7 +876,7 @@ def main():
                          "bound_us": round(pre_bound_s * 1e6, 3), "alg_bytes": pre_bytes, "alg_flops": pre_flops,
                          "traffic": NCU_TRAFFIC["prefill_8k_call"], "traffic_scope": "all kernels of one call",
                          "traffic_warm_caches": NCU_TRAFFIC["prefill_8k_call_warm"],
-                         "kernel_us_warm": {"prep": 56.3, "seg_local": 46.8, "seg_chain": 8.4, "seg_out": 17.9},
+                         "kernel_us_warm": {"prep": 55.8, "seg_local": 44.2, "seg_chain": 8.3, "seg_out": 17.7},
                          "critical_path_us": PREFILL_8K_CRITICAL_PATH_US,
                          "peak_source": peak_src},
             "routes": pre_routes,
